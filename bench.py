@@ -1,0 +1,534 @@
+"""Multi-LoRA shrink+expand benchmark (BASELINE.json metric) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: one decode batch of 256 tokens at Llama-3-8B
+projection shapes with 128 resident rank-16 adapters, adapter ids Zipf(1.1); the
+three projections fused QKV (4096 -> 4096/1024/1024), gate/up (4096 -> 2 x 14336)
+and down (14336 -> 4096).  x ~ N(0,1), A ~ N(0,1/K), B ~ N(0,1/r), scale 2.0, all
+BF16, seeded synthetic data.  One step = device grouping of the batch by adapter
++ shrink + expand of the three projections.
+
+``value``   tokens/s of the step replayed as a CUDA graph with inputs resident in
+            HBM; L2 is flushed (a write larger than L2) before every timed step and
+            the flush is outside the per-step CUDA events.
+``e2e``     the same step through the public Python API with pinned host buffers:
+            H2D of the step's activations and routing, D2H of the three outputs.
+``roofline`` the dominant kernel's algorithmic bytes / its mean event time, against
+            the measured HBM copy bandwidth in MEASURED_PEAKS.json.
+``cpu_baseline`` the FP32 einsum over per-adapter gathers (the oracle port) on the
+            host cores, on a bounded sample of steps (rank 0, N=1 only).
+
+With N>1 (torchrun) every rank runs an independent replica of the workload
+(replicas only: config 1 has no cross-GPU exchange); value = all ranks' tokens /
+max over ranks of the device time.  ``--impl reference`` times the CPU oracle port
+on the same workload (rank 0 only).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+T_TOKENS = 256
+N_SLOTS = 128
+RANK = 16
+ZIPF_S = 1.1
+SCALE = 2.0
+PROJECTIONS = (  # name, in_dim, slice widths
+    ("qkv_proj", 4096, (4096, 1024, 1024)),
+    ("gate_up_proj", 4096, (14336, 14336)),
+    ("down_proj", 14336, (4096,)),
+)
+
+
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=300)
+    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--seed", type=int, default=1234)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--profile", action="store_true", help="short run for ncu (no sampling/baselines)")
+    return p.parse_args()
+
+
+# ----------------------------------------------------------------------------- workload
+def zipf_slots(rng, tokens, slots, s):
+    ranks = np.arange(1, slots + 1, dtype=np.float64)
+    p = ranks**-s
+    return rng.choice(slots, size=tokens, p=p / p.sum()).astype(np.int32)
+
+
+class Projection:
+    def __init__(self, name, k, widths, device, gen):
+        import torch
+
+        self.name, self.K, self.widths = name, k, widths
+        self.S, self.N = len(widths), sum(widths)
+        S, N, K = self.S, self.N, k
+        self.a = (torch.randn(N_SLOTS, S * RANK, K, generator=gen, device=device) / K**0.5).bfloat16()
+        self.b = (torch.randn(N_SLOTS * N * RANK, generator=gen, device=device) / RANK**0.5).bfloat16()
+        self.b_offsets = torch.arange(N_SLOTS, dtype=torch.int64, device=device) * (N * RANK)
+        self.b_strides = torch.full((N_SLOTS,), RANK, dtype=torch.int32, device=device)
+        self.ranks = torch.full((N_SLOTS,), RANK, dtype=torch.int32, device=device)
+        self.scales = torch.full((N_SLOTS,), SCALE, dtype=torch.float32, device=device)
+        self.slice_offsets = torch.tensor(np.cumsum((0, *widths)), dtype=torch.int32, device=device)
+        self.z = torch.zeros(T_TOKENS, S * RANK, dtype=torch.bfloat16, device=device)
+        self.y = torch.zeros(T_TOKENS, N, dtype=torch.bfloat16, device=device)
+
+    def b_rows(self, g):
+        """Host copy of slot g's B rows [N, r] (for the CPU oracle)."""
+        n = self.N * RANK
+        return self.b_host[g * n : (g + 1) * n].view(self.N, RANK)
+
+    def shrink_bytes(self, touched, t_active):
+        return t_active * self.K * 2 + touched * self.S * RANK * self.K * 2 + t_active * self.S * RANK * 2
+
+    def expand_bytes(self, touched, t_active):
+        return touched * self.N * RANK * 2 + t_active * self.N * 2 * 2 + t_active * self.S * RANK * 2
+
+    def flops(self, t_active):
+        return t_active * 2 * RANK * (self.S * self.K + self.N)
+
+
+class Workload:
+    def __init__(self, device, seed):
+        import torch
+
+        from loraforge_b200.ops.grouping import empty_routing
+
+        gen = torch.Generator(device=device).manual_seed(seed)
+        rng = np.random.default_rng(seed)
+        self.device = device
+        self.slots_np = zipf_slots(rng, T_TOKENS, N_SLOTS, ZIPF_S)
+        self.slots = torch.from_numpy(self.slots_np).to(device)
+        self.x_in = torch.randn(T_TOKENS, 4096, generator=gen, device=device).bfloat16()
+        self.x_down = torch.randn(T_TOKENS, 14336, generator=gen, device=device).bfloat16()
+        self.projections = [Projection(n, k, w, device, gen) for n, k, w in PROJECTIONS]
+        self.routing = empty_routing(T_TOKENS, device)
+        self.touched = int(len(np.unique(self.slots_np[self.slots_np >= 0])))
+        self.t_active = int((self.slots_np >= 0).sum())
+
+    def x_of(self, p):
+        return self.x_down if p.K == 14336 else self.x_in
+
+    def bytes_per_step(self):
+        return sum(
+            p.shrink_bytes(self.touched, self.t_active) + p.expand_bytes(self.touched, self.t_active)
+            for p in self.projections
+        ) + T_TOKENS * 4
+
+    def flops_per_step(self):
+        return sum(p.flops(self.t_active) for p in self.projections)
+
+
+def run_step(w, events=None):
+    """Grouping + shrink/expand of the three projections through the public API."""
+    from loraforge_b200.ops import row_expand, row_shrink
+    from loraforge_b200.ops.grouping import group_tokens
+
+    r = group_tokens(w.slots, N_SLOTS, chunk=16, out=w.routing)
+    for i, p in enumerate(w.projections):
+        if events is not None:
+            events[i][0].record()
+        row_shrink(w.x_of(p), p.a, p.z, w.slots, p.ranks, num_slices=p.S, max_rank=RANK)
+        if events is not None:
+            events[i][1].record()
+        row_expand(
+            p.z, p.b, p.y, b_offsets=p.b_offsets, b_strides=p.b_strides, ranks=p.ranks,
+            scales=p.scales, segment_indptr=r.segment_indptr, segment_slots=r.segment_slots,
+            token_indices=r.token_indices, slice_offsets=p.slice_offsets,
+            segment_count=r.segment_count,
+        )
+        if events is not None:
+            events[i][2].record()
+
+
+LAUNCHES_PER_STEP = 1 + 2 * len(PROJECTIONS)
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """NVML SM-clock / throttle-reason sampling during the timed region (read-only)."""
+
+    REASONS = {
+        0x0000000000000004: "sw_power_cap",
+        0x0000000000000008: "hw_slowdown",
+        0x0000000000000020: "sw_thermal_slowdown",
+        0x0000000000000040: "hw_thermal_slowdown",
+        0x0000000000000080: "hw_power_brake_slowdown",
+    }
+
+    def __init__(self, index):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            uuid = getattr(torch.cuda.get_device_properties(index), "uuid", None)
+            if uuid is not None:
+                self._h = pynvml.nvmlDeviceGetHandleByUUID(f"GPU-{uuid}")
+            else:
+                self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self._reasons_fn = getattr(
+                pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None
+            ) or getattr(pynvml, "nvmlDeviceGetCurrentClocksThrottleReasons")
+        except Exception:  # NVML unavailable: report no clock record
+            self._nvml = None
+
+    def _run(self):
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                mask = self._reasons_fn(self._h)
+                for bit, name in self.REASONS.items():
+                    if mask & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            self._stop.wait(0.01)
+
+    def __enter__(self):
+        if self._nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def record(self):
+        if not self.samples:
+            return None
+        return {
+            "sm_mhz": statistics.median(self.samples),
+            "sm_max_mhz": self.max_mhz,
+            "samples": len(self.samples),
+            "reasons": sorted(self.reasons),
+        }
+
+
+# ----------------------------------------------------------------------------- timing
+def measured_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def time_graph(w, steps, warmup, flush):
+    """Replay the captured step `steps` times; per-step and per-kernel CUDA events."""
+    import torch
+
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            run_step(w)
+    torch.cuda.current_stream().wait_stream(stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in PROJECTIONS]
+    kernel_graphs = []
+    with torch.cuda.graph(graph):
+        run_step(w)
+    # Per-kernel timing uses a second graph with events between launches.
+    graph_ev = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph_ev):
+        run_step(w, events=ev)
+    kernel_graphs.append(graph_ev)
+    for _ in range(warmup):
+        flush.zero_()
+        graph.replay()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    for i in range(steps):
+        flush.zero_()
+        starts[i].record()
+        graph.replay()
+        ends[i].record()
+    torch.cuda.synchronize()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    # Kernel breakdown: shrink/expand time per projection, flushed before each step.
+    per_kernel = {f"{p[0]}.{k}": [] for p in PROJECTIONS for k in ("shrink", "expand")}
+    for _ in range(min(steps, 100)):
+        flush.zero_()
+        graph_ev.replay()
+        torch.cuda.synchronize()
+        for (name, _, _), (e0, e1, e2) in zip(PROJECTIONS, ev):
+            per_kernel[f"{name}.shrink"].append(e0.elapsed_time(e1))
+            per_kernel[f"{name}.expand"].append(e1.elapsed_time(e2))
+    del graph, kernel_graphs
+    return step_ms, {k: statistics.mean(v) for k, v in per_kernel.items()}
+
+
+def time_e2e(w, steps, warmup):
+    """Public API with host buffers: H2D inputs, the step, D2H outputs, per step."""
+    import torch
+
+    host_x_in = w.x_in.cpu().pin_memory()
+    host_x_down = w.x_down.cpu().pin_memory()
+    host_slots = w.slots.cpu().pin_memory()
+    host_out = [torch.empty(p.y.shape, dtype=p.y.dtype).pin_memory() for p in w.projections]
+    h2d = host_x_in.numel() * 2 + host_x_down.numel() * 2 + host_slots.numel() * 4
+    d2h = sum(t.numel() * 2 for t in host_out)
+
+    def one():
+        w.x_in.copy_(host_x_in, non_blocking=True)
+        w.x_down.copy_(host_x_down, non_blocking=True)
+        w.slots.copy_(host_slots, non_blocking=True)
+        run_step(w)
+        for p, h in zip(w.projections, host_out):
+            h.copy_(p.y, non_blocking=True)
+
+    for _ in range(warmup):
+        one()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        one()
+    end.record()
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) / steps, h2d, d2h
+
+
+def cpu_baseline(w, budget_s=15.0):
+    """FP32 einsum over per-adapter gathers on the host (oracle port), bounded sample."""
+    import torch
+
+    from oracle.cpu_reference import lora_delta_fp32
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    slots = w.slots_np
+    x_in = w.x_in.float().cpu()
+    x_down = w.x_down.float().cpu()
+    hosts = []
+    for p in w.projections:
+        p.b_host = p.b.cpu()
+        hosts.append((p, p.a.cpu()))
+    ranks = np.full(N_SLOTS, RANK)
+    scales = np.full(N_SLOTS, SCALE)
+
+    def step():
+        for p, a_host in hosts:
+            x = x_down if p.K == 14336 else x_in
+            lora_delta_fp32(x, a_host, p.b_rows, slots, ranks, scales, p.slice_offsets.cpu().numpy())
+
+    step()  # warm-up
+    times = []
+    begin = time.perf_counter()
+    while time.perf_counter() - begin < budget_s and len(times) < 50:
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    per_step = statistics.median(times)
+    return {
+        "value": T_TOKENS / per_step,
+        "unit": "tokens/s",
+        "cores": threads,
+        "kind": "port",
+        "sample": f"{len(times)} full steps (3 projections x {T_TOKENS} tokens), median",
+    }
+
+
+# ----------------------------------------------------------------------------- main
+def init_distributed():
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def max_over_ranks(value, world):
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    import torch
+
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def main():
+    args = parse_args()
+    import torch
+
+    config = {
+        "workload": "config1: decode BGMV, Llama-3-8B qkv/gate_up/down, 256 tokens, "
+        "128 adapters r=16, Zipf(1.1)",
+        "tokens": T_TOKENS,
+        "adapters": N_SLOTS,
+        "rank": RANK,
+        "l2": "flushed before every timed step (256 MiB write, outside the step events)",
+    }
+    if args.impl == "reference":
+        return main_reference(args, config)
+    world, rank, local = init_distributed()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    w = Workload(device, args.seed + rank)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
+    steps, warmup = args.steps, max(3, args.warmup)
+    barrier(world)
+    with ClockSampler(local) as clocks:
+        step_ms, per_kernel = time_graph(w, steps, warmup, flush)
+    barrier(world)
+    total_ms = max_over_ranks(sum(step_ms), world)
+    ms_per_step = total_ms / steps
+    value = world * T_TOKENS * steps / (total_ms / 1e3)
+    peak, peak_kind = measured_peaks()
+    dominant = max(per_kernel, key=per_kernel.get)
+    name, kind = dominant.split(".")
+    p = next(p for p in w.projections if p.name == name)
+    alg = (p.shrink_bytes if kind == "shrink" else p.expand_bytes)(w.touched, w.t_active)
+    achieved = alg / (per_kernel[dominant] * 1e-3) / 1e9
+    result = {
+        "metric": "multi-LoRA shrink+expand tokens/s (decode, config 1)",
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": steps,
+        "warmup": warmup,
+        "ms_per_step": ms_per_step,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded; BASELINE config 1 shapes and distributions)",
+        "config": config | {"parallelism": f"replicas{world}"},
+        "hbm_gbs_step": w.bytes_per_step() / (ms_per_step * 1e-3) / 1e9,
+        "bytes_per_step": w.bytes_per_step(),
+        "flops_per_step": w.flops_per_step(),
+        "kernel_ms": per_kernel,
+        "roofline": {
+            "bound": "hbm",
+            "kernel": dominant,
+            "achieved": achieved,
+            "peak": peak,
+            "unit": "GB/s",
+            "frac": achieved / peak,
+            "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+            "traffic": None,
+        },
+        "gpu_launches": LAUNCHES_PER_STEP * steps,
+        "clocks": clocks.record(),
+    }
+    if not args.no_e2e and not args.profile:
+        e2e_ms, h2d, d2h = time_e2e(w, max(10, steps // 10), 3)
+        e2e_ms = max_over_ranks(e2e_ms, world)
+        result["e2e"] = {
+            "value": world * T_TOKENS / (e2e_ms * 1e-3),
+            "unit": "tokens/s",
+            "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h,
+        }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.profile:
+        result["cpu_baseline"] = cpu_baseline(w)
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def main_reference(args, config):
+    """CPU oracle port of the reference path on the host cores (rank 0 only)."""
+    import torch
+
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    device = torch.device("cpu")
+    w = Workload.__new__(Workload)
+    gen = torch.Generator().manual_seed(args.seed)
+    rng = np.random.default_rng(args.seed)
+    w.slots_np = zipf_slots(rng, T_TOKENS, N_SLOTS, ZIPF_S)
+    w.x_in = torch.randn(T_TOKENS, 4096, generator=gen).bfloat16()
+    w.x_down = torch.randn(T_TOKENS, 14336, generator=gen).bfloat16()
+    w.projections = [_host_projection(n, k, wd, gen) for n, k, wd in PROJECTIONS]
+    budget = max(10.0, min(120.0, 2.0 * (args.steps + args.warmup)))
+    base = cpu_baseline(w, budget_s=budget)
+    print(
+        json.dumps(
+            {
+                "impl": "reference",
+                "metric": "multi-LoRA shrink+expand tokens/s (decode, config 1)",
+                "value": base["value"],
+                "unit": "tokens/s",
+                "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
+                "steps": args.steps,
+                "warmup": args.warmup,
+                "ms_per_step": 1e3 * T_TOKENS / base["value"],
+                "higher_is_better": True,
+                "scaling": "weak",
+                "vs_baseline": None,
+                "dtype": "f32",
+                "data": "synthetic (seeded; BASELINE config 1 shapes and distributions)",
+                "config": config | {"parallelism": "host cores"},
+                "cpu_baseline": base,
+                "e2e": {"value": base["value"], "unit": "tokens/s",
+                        "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            }
+        ),
+        flush=True,
+    )
+
+
+def _host_projection(name, k, widths, gen):
+    import torch
+
+    p = Projection.__new__(Projection)
+    p.name, p.K, p.widths, p.S, p.N = name, k, widths, len(widths), sum(widths)
+    p.a = (torch.randn(N_SLOTS, p.S * RANK, k, generator=gen) / k**0.5).bfloat16()
+    p.b = (torch.randn(N_SLOTS * p.N * RANK, generator=gen) / RANK**0.5).bfloat16()
+    p.slice_offsets = torch.tensor(np.cumsum((0, *widths)), dtype=torch.int32)
+    return p
+
+
+if __name__ == "__main__":
+    main()

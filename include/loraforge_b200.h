@@ -1,0 +1,157 @@
+/*
+ * loraforge_b200 — C ABI of the B200 (sm_100a) multi-LoRA shrink/expand path.
+ *
+ * Every entry point takes raw device pointers, element counts and strides and a
+ * cudaStream_t passed as `void*`; none of them allocates, synchronises or reads
+ * device memory on the host. Each returns 0 on success or a negative LF_E_* code;
+ * lf_last_error_string() then describes the failure (thread-local).
+ *
+ * Device metadata (slots, ranks, offsets, segment tables) is trusted the same way
+ * the reference trusts it, with one difference: every kernel clamps the device
+ * segment count to the host-known table capacity and skips out-of-range slot ids
+ * instead of reading out of bounds.
+ *
+ * Element types: LF_F32 = 0, LF_F16 = 1, LF_BF16 = 2.
+ * Reference paths below are relative to the lishenghui/loraforge source tree.
+ */
+#ifndef LORAFORGE_B200_H
+#define LORAFORGE_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  LF_OK = 0,
+  LF_E_INVALID = -1,  /* structural argument error (shape, stride, alignment) */
+  LF_E_CUDA = -2,     /* a CUDA runtime call or kernel launch failed */
+  LF_E_UNSUPPORTED = -3,
+};
+
+enum { LF_F32 = 0, LF_F16 = 1, LF_BF16 = 2 };
+
+/* Library version (major*10000 + minor*100 + patch). */
+int lf_version(void);
+
+/* Description of the last failure on this host thread ("" if none). */
+const char* lf_last_error_string(void);
+
+/*
+ * Stable grouping of tokens by adapter slot, on device, in one CTA.
+ *   token_indices[0:n_active]  = active tokens sorted by slot, ties by token index;
+ *   token_indices[n_active:T]  = tokens with slot outside [0, num_slots), in order;
+ *   segments: for each slot with tokens (ascending), ceil(count/chunk) segments of
+ *   at most `chunk` tokens (chunk <= 0: one segment per slot);
+ *   segment_indptr[0..nseg] offsets into token_indices, segment_slots[nseg],
+ *   segment_count[0] = nseg.  Buffers must hold T+1 / T / T entries.
+ * Replaces SGLang 0.5.22 ChunkedSgmvLoRABackend.prepare_lora_batch's grouping
+ * (called at src/loraforge/integrations/_sglang_fleet.py:250-257); the layout of
+ * its outputs is the one row_expand consumes (src/loraforge/ops/lora_rows.py:115-131).
+ */
+int lf_group_tokens(const int32_t* slots, int64_t num_tokens, int32_t num_slots,
+                    int32_t chunk, int32_t* segment_indptr, int32_t* segment_slots,
+                    int32_t* token_indices, int32_t* segment_count, void* stream);
+
+/*
+ * Retained-rank BF16 shrink: z[t, s*r+k] = bf16(sum_i a[g, s*r+k, i] * x[t, i]) for
+ * g = slots[t] >= 0, r = ranks[g] in 1..max_rank, s < num_slices, k < r.  Other z
+ * entries are left unchanged.  x row stride `x_stride` (elements), A contiguous
+ * [num_slots, num_slices*capacity, width], z contiguous [T, num_slices*capacity].
+ * Replaces src/loraforge/ops/csrc/lora_rows.cu:172-186 (`shrink`, bound by
+ * src/loraforge/ops/lora_rows.py:106-109) and the fleet form
+ * src/loraforge/ops/csrc/rowexpand.cu:87-97 (num_slices up to 4).
+ */
+int lf_row_shrink(const void* x, int64_t x_stride, const void* a, void* z,
+                  const int32_t* slots, const int32_t* ranks, int64_t num_tokens,
+                  int64_t width, int32_t num_slots, int32_t num_slices,
+                  int32_t capacity, int32_t max_rank, void* stream);
+
+/*
+ * Compact-B RowExpand: for each active segment (<= 16 tokens, one slot g with rank
+ * r in 1..64) and each output column n of slice s:
+ *   acc = sum_{k < bucket} zf[k] * B[b_offsets[g] + n*bucket + k]   (k ascending,
+ *         zf[k] = z[t, s*r+k] for k < r else 0),
+ *   y[t, n] = bf16(y[t, n] + bf16(acc * scales[g])).
+ * Same arithmetic, in the same order, as src/loraforge/ops/csrc/lora_rows.cu:67-162
+ * (`expand` at :188-209) and src/loraforge/ops/csrc/rowexpand.cu:33-86.
+ * row_tile in {2,4,8,16} splits segments into sub-tiles (work split only).
+ * `threads` in {128, 256}; `blocks` is the persistent grid size.
+ */
+int lf_row_expand(const void* z, const void* b, const int64_t* b_offsets,
+                  const int32_t* b_strides, void* y, int64_t y_stride,
+                  const int32_t* segment_indptr, const int32_t* segment_slots,
+                  const int32_t* token_indices, const int32_t* ranks,
+                  const float* scales, const int32_t* slice_offsets,
+                  const int32_t* segment_count, int64_t num_tokens, int32_t out_width,
+                  int32_t num_slices, int32_t capacity, int32_t num_slots,
+                  int32_t max_segments, int32_t blocks, int32_t threads,
+                  int32_t row_tile, void* stream);
+
+/*
+ * Padded-A decode shrink (SGLang "compatible" layout): A [num_slots, S*Rmax, width]
+ * contiguous, z [T, S*Rmax] contiguous; rank = min(ranks[g], Rmax);
+ * z[t, s*rank+k] = dtype(sum_i A[g, s*rank+k, i] * x[t, i]) for k < rank.  Other z
+ * entries are not written (the Python layer zero-fills z first).
+ * index_bits = 32 or 64 for ranks / token_map.  Replaces the Triton
+ * shrink_dot_kernel / shrink_kernel+reduce_kernel launched by
+ * src/loraforge/ops/gemv.py:46-127.
+ */
+int lf_bgmv_shrink(int32_t dtype, const void* x, int64_t x_stride, const void* a,
+                   void* z, const void* ranks, const void* token_map,
+                   int32_t index_bits, int64_t num_tokens, int64_t width,
+                   int32_t num_slots, int32_t num_slices, int32_t rmax, void* stream);
+
+/*
+ * Padded-B decode expand: B [num_slots, out_width, Rmax] contiguous, z packed
+ * [T, S*Rmax]; for column n in slice s (offsets[s] <= n < offsets[s+1]):
+ *   y[t, n] = dtype(y[t, n] + dtype(scale_g * sum_{k<rank} z[t, s*rank+k] B[g,n,k])).
+ * Rank-0 tokens are untouched.  scales dtype = scale_dtype (LF_*), offsets and
+ * ranks/token_map use offset_bits / index_bits (32 or 64).
+ * Replaces the Triton expand_dot_kernel / expand_kernel launched by
+ * src/loraforge/ops/gemv.py:130-238.
+ */
+int lf_bgmv_expand(int32_t dtype, const void* z, const void* b, const void* ranks,
+                   const void* scales, int32_t scale_dtype, const void* token_map,
+                   int32_t index_bits, const void* offsets, int32_t offset_bits,
+                   void* y, int64_t y_stride0, int64_t y_stride1, int64_t num_tokens,
+                   int32_t out_width, int32_t num_slots, int32_t num_slices,
+                   int32_t rmax, void* stream);
+
+/* Per-slice operand descriptor for the vLLM padded layouts (up to 8 slices). */
+typedef struct lf_slice_desc {
+  const void* ptr;     /* slice base: A [slots, (1,) rank, width] or B [slots, (1,) n, rank] */
+  int64_t slot_stride; /* elements between slots */
+  int64_t row_stride;  /* elements between rows (rank rows for A, n rows for B) */
+  int64_t rows;        /* rank (A) or n (B) */
+} lf_slice_desc;
+
+/*
+ * vLLM BGMV shrink: out[s, t, :rank] (fp32, contiguous [S, T, rank]) =
+ *   scale * A_s[routes[t]] @ x[t]; routes outside [0, num_slots) leave out untouched
+ *   (the Python layer zero-fills out first, so they read as zeros).  Deterministic (no
+ * atomics).  Replaces src/loraforge/ops/vllm_gemv.py:49-101 and
+ * src/loraforge/ops/_vllm_gemv_kernels.py:12-53.
+ */
+int lf_vllm_shrink(int32_t dtype, const void* x, int64_t x_stride,
+                   const lf_slice_desc* slices, int32_t num_slices, int32_t num_slots,
+                   float* out, const int32_t* routes, int64_t num_tokens, int64_t width,
+                   int32_t rank, float scale, void* stream);
+
+/*
+ * vLLM BGMV expand: y[t, offset + o_s + n] = dtype((add ? y : 0) + B_s[g] @ v[s, t])
+ * with FP32 accumulation and one final cast; routes[t] < 0 rows are untouched.
+ * Replaces src/loraforge/ops/vllm_gemv.py:107-159 and
+ * src/loraforge/ops/_vllm_gemv_kernels.py:57-92.
+ */
+int lf_vllm_expand(int32_t dtype, const float* v, const lf_slice_desc* slices,
+                   int32_t num_slices, int32_t num_slots, void* y, int64_t y_stride,
+                   const int32_t* routes, int64_t num_tokens, int32_t rank,
+                   int64_t offset, int32_t add, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LORAFORGE_B200_H */

@@ -1,0 +1,179 @@
+// Device-side stable grouping of decode/prefill tokens by adapter slot.
+//
+// One CTA of 1024 threads: a shared-memory histogram of slot ids, two block-wide
+// exclusive scans (token offsets per slot and segment offsets per slot) and a
+// stable scatter done by one warp with __match_any_sync ranks.  The result is the
+// routing table SGLang's prepare_lora_batch produces for the reference
+// (seg_indptr / weight_indices / permutation, consumed at
+// src/loraforge/integrations/_sglang_fleet.py:390-407), computed without a host
+// round trip so it can live inside a CUDA graph.
+#include "launch.cuh"
+
+namespace lfb {
+namespace {
+
+constexpr int kGroupThreads = 1024;
+constexpr int kGroupWarps = kGroupThreads / 32;
+
+// Exclusive scan of two int arrays of length n in shared memory, in place, with all
+// 1024 threads.  Returns the totals through *total_a / *total_b (shared).
+__device__ void block_exclusive_scan2(int* a, int* b, int n, int* warp_a, int* warp_b,
+                                      int* total_a, int* total_b) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int per = (n + kGroupThreads - 1) / kGroupThreads;
+  const int begin = min(n, tid * per), end = min(n, begin + per);
+  int sa = 0, sb = 0;
+  for (int i = begin; i < end; ++i) {
+    sa += a[i];
+    sb += b[i];
+  }
+  int ia = sa, ib = sb;  // warp inclusive scan
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int va = __shfl_up_sync(0xffffffffu, ia, d);
+    const int vb = __shfl_up_sync(0xffffffffu, ib, d);
+    if (lane >= d) {
+      ia += va;
+      ib += vb;
+    }
+  }
+  if (lane == 31) {
+    warp_a[warp] = ia;
+    warp_b[warp] = ib;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int wa = warp_a[lane], wb = warp_b[lane];
+    int xa = wa, xb = wb;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int va = __shfl_up_sync(0xffffffffu, xa, d);
+      const int vb = __shfl_up_sync(0xffffffffu, xb, d);
+      if (lane >= d) {
+        xa += va;
+        xb += vb;
+      }
+    }
+    warp_a[lane] = xa - wa;  // exclusive warp offsets
+    warp_b[lane] = xb - wb;
+    if (lane == 31) {
+      *total_a = xa;
+      *total_b = xb;
+    }
+  }
+  __syncthreads();
+  int ra = warp_a[warp] + ia - sa, rb = warp_b[warp] + ib - sb;
+  for (int i = begin; i < end; ++i) {
+    const int va = a[i], vb = b[i];
+    a[i] = ra;
+    b[i] = rb;
+    ra += va;
+    rb += vb;
+  }
+  __syncthreads();
+}
+
+// Shared memory: start[num_slots + 2] (bucket num_slots collects inactive tokens,
+// num_slots + 1 is a dummy for padding lanes), segbase[num_slots + 1], scan scratch,
+// and, when it fits, a cache of the tokens' bucket ids.
+__global__ void __launch_bounds__(kGroupThreads)
+group_tokens_kernel(const int32_t* __restrict__ slots, int T, int num_slots, int chunk,
+                    int32_t* __restrict__ indptr, int32_t* __restrict__ seg_slots,
+                    int32_t* __restrict__ perm, int32_t* __restrict__ seg_count,
+                    int cache_tokens) {
+  extern __shared__ int smem[];
+  int* start = smem;                       // num_slots + 2
+  int* segbase = start + num_slots + 2;    // num_slots + 1
+  int* warp_a = segbase + num_slots + 1;   // 32
+  int* warp_b = warp_a + kGroupWarps;      // 32
+  int* totals = warp_b + kGroupWarps;      // 2
+  int* cache = totals + 2;                 // T when cache_tokens
+  const int tid = threadIdx.x;
+
+  for (int s = tid; s < num_slots + 2; s += kGroupThreads) start[s] = 0;
+  __syncthreads();
+  for (int t = tid; t < T; t += kGroupThreads) {
+    const int s = slots[t];
+    const int bucket = (s >= 0 && s < num_slots) ? s : num_slots;
+    if (cache_tokens) cache[t] = bucket;
+    atomicAdd(&start[bucket], 1);
+  }
+  __syncthreads();
+  for (int s = tid; s < num_slots; s += kGroupThreads) {
+    const int c = start[s];
+    segbase[s] = chunk > 0 ? (c + chunk - 1) / chunk : (c > 0 ? 1 : 0);
+  }
+  if (tid == 0) segbase[num_slots] = 0;
+  __syncthreads();
+  // Scan buckets 0..num_slots (the inactive bucket starts at n_active) and the
+  // per-slot segment counts.
+  block_exclusive_scan2(start, segbase, num_slots + 1, warp_a, warp_b, &totals[0], &totals[1]);
+  const int n_active = start[num_slots];
+  const int nseg = segbase[num_slots];
+  for (int s = tid; s < num_slots; s += kGroupThreads) {
+    const int begin = start[s];
+    const int first = segbase[s];
+    const int pieces = segbase[s + 1] - first;
+    for (int j = 0; j < pieces; ++j) {
+      indptr[first + j] = begin + (chunk > 0 ? j * chunk : 0);
+      seg_slots[first + j] = s;
+    }
+  }
+  if (tid == 0) {
+    indptr[nseg] = n_active;
+    *seg_count = nseg;
+  }
+  __syncthreads();
+  // Stable scatter: warp 0 walks the tokens in order, 32 at a time; lanes with the
+  // same bucket get consecutive positions in token order.
+  if (tid < 32) {
+    const int lane = tid;
+    const unsigned lower = (1u << lane) - 1u;
+    for (int base = 0; base < T; base += 32) {
+      const int t = base + lane;
+      int bucket = num_slots + 1;
+      if (t < T) {
+        if (cache_tokens) {
+          bucket = cache[t];
+        } else {
+          const int s = slots[t];
+          bucket = (s >= 0 && s < num_slots) ? s : num_slots;
+        }
+      }
+      const unsigned same = __match_any_sync(0xffffffffu, bucket);
+      const int pos = start[bucket] + __popc(same & lower);
+      __syncwarp();
+      if (lane == __ffs(same) - 1) start[bucket] += __popc(same);
+      __syncwarp();
+      if (t < T) perm[pos] = t;
+    }
+  }
+}
+
+}  // namespace
+}  // namespace lfb
+
+extern "C" int lf_group_tokens(const int32_t* slots, int64_t num_tokens, int32_t num_slots,
+                               int32_t chunk, int32_t* segment_indptr,
+                               int32_t* segment_slots, int32_t* token_indices,
+                               int32_t* segment_count, void* stream) {
+  using namespace lfb;
+  if (num_tokens < 0 || num_tokens >= (int64_t(1) << 31))
+    return fail(LF_E_INVALID, "group_tokens: token count must fit signed int32");
+  if (num_slots < 1 || num_slots > 16384)
+    return fail(LF_E_INVALID, "group_tokens: num_slots must be in 1..16384");
+  if (!segment_indptr || !segment_count || (num_tokens && (!slots || !segment_slots || !token_indices)))
+    return fail(LF_E_INVALID, "group_tokens: null buffer");
+  const int T = static_cast<int>(num_tokens);
+  const size_t fixed = sizeof(int) * (size_t(num_slots) * 2 + 3 + 2 * kGroupWarps + 2);
+  const size_t limit = 200 * 1024;
+  if (fixed > limit) return fail(LF_E_INVALID, "group_tokens: too many slots");
+  const int cache = fixed + sizeof(int) * size_t(T) <= limit ? 1 : 0;
+  const size_t bytes = fixed + (cache ? sizeof(int) * size_t(T) : 0);
+  static unsigned long long flags = 0;
+  if (int rc = ensure_smem(group_tokens_kernel, int(limit), &flags)) return rc;
+  group_tokens_kernel<<<1, kGroupThreads, bytes, static_cast<cudaStream_t>(stream)>>>(
+      slots, T, num_slots, chunk, segment_indptr, segment_slots, token_indices,
+      segment_count, cache);
+  return check_launch("group_tokens");
+}

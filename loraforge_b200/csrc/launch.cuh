@@ -1,0 +1,44 @@
+// Launch helpers: per-device one-time kernel attributes and cluster launches.
+#pragma once
+
+#include "common.cuh"
+
+namespace lfb {
+
+// Raise a kernel's dynamic shared-memory limit once per device.  `flags` is a
+// per-kernel bitmask of devices already configured (devices 0..63).
+template <typename Kernel>
+inline int ensure_smem(Kernel kernel, int bytes, unsigned long long* flags) {
+  if (bytes <= 48 * 1024) return LF_OK;
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return check_launch("cudaGetDevice");
+  const unsigned long long bit = 1ull << (device & 63);
+  if (*flags & bit) return LF_OK;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) !=
+      cudaSuccess)
+    return check_launch("cudaFuncSetAttribute");
+  *flags |= bit;
+  return LF_OK;
+}
+
+// Launch `kernel` with a (1, 1, cluster_z) thread-block cluster.
+template <typename... Params, typename... Args>
+inline cudaError_t launch_cluster_z(void (*kernel)(Params...), dim3 grid, dim3 block,
+                                    size_t smem, cudaStream_t stream, int cluster_z,
+                                    Args&&... args) {
+  cudaLaunchConfig_t config = {};
+  config.gridDim = grid;
+  config.blockDim = block;
+  config.dynamicSmemBytes = smem;
+  config.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = cluster_z;
+  config.attrs = attr;
+  config.numAttrs = 1;
+  return cudaLaunchKernelEx(&config, kernel, std::forward<Args>(args)...);
+}
+
+}  // namespace lfb

@@ -1,0 +1,80 @@
+"""Device-side routing metadata: tokens grouped by adapter slot.
+
+Produces the ``segment_indptr / segment_slots / token_indices / segment_count``
+tables that ``row_expand`` consumes (src/loraforge/ops/lora_rows.py:115-131) —
+the role SGLang's ``prepare_lora_batch`` plays for the reference
+(src/loraforge/integrations/_sglang_fleet.py:250-257) — on the GPU, with no host
+read of the routing, so the whole routing step can be captured in a CUDA graph.
+Grouping is stable: active tokens are ordered by slot, ties by token index.
+"""
+
+from __future__ import annotations
+
+from typing import NamedTuple
+
+from loraforge_b200 import _native
+
+
+class Routing(NamedTuple):
+    segment_indptr: object  # int32 [T + 1]
+    segment_slots: object  # int32 [T]
+    token_indices: object  # int32 [T]
+    segment_count: object  # int32 [1]
+
+
+def empty_routing(num_tokens: int, device) -> Routing:
+    """Fixed-address routing buffers for ``num_tokens`` tokens (reuse across replays)."""
+    import torch
+
+    n = max(1, num_tokens)
+    return Routing(
+        torch.zeros(n + 1, dtype=torch.int32, device=device),
+        torch.zeros(n, dtype=torch.int32, device=device),
+        torch.zeros(n, dtype=torch.int32, device=device),
+        torch.zeros(1, dtype=torch.int32, device=device),
+    )
+
+
+def group_tokens(slots, num_slots: int, *, chunk: int = 16, out: Routing | None = None) -> Routing:
+    """Group tokens by ``slots`` (int32 [T], -1 = no adapter) into <= ``chunk`` token segments.
+
+    ``chunk <= 0`` gives one segment per active slot.  Writes into ``out`` when given
+    (every buffer must have room for T tokens), else allocates.
+    """
+    import torch
+
+    if not isinstance(slots, torch.Tensor):
+        raise TypeError("slots must be a torch.Tensor")
+    if slots.ndim != 1 or slots.dtype != torch.int32 or not slots.is_contiguous():
+        raise ValueError("slots must be a contiguous int32 vector")
+    if slots.device.type != "cuda":
+        raise ValueError("slots must be on a CUDA device")
+    if type(num_slots) is not int or not 1 <= num_slots <= 16384:
+        raise ValueError("num_slots must be in 1..16384")
+    if type(chunk) is not int:
+        raise ValueError("chunk must be an integer")
+    T = slots.numel()
+    if out is None:
+        out = empty_routing(T, slots.device)
+    for buf, need in zip(out, (T + 1, T, T, 1)):
+        if (
+            buf.dtype != torch.int32
+            or buf.device != slots.device
+            or not buf.is_contiguous()
+            or buf.numel() < need
+        ):
+            raise ValueError("routing buffers must be contiguous int32 with room for every token")
+    with torch.cuda.device(slots.device):
+        _native.call(
+            "lf_group_tokens",
+            slots.data_ptr(),
+            T,
+            num_slots,
+            chunk,
+            out.segment_indptr.data_ptr(),
+            out.segment_slots.data_ptr(),
+            out.token_indices.data_ptr(),
+            out.segment_count.data_ptr(),
+            _native.stream_of(slots.device),
+        )
+    return out

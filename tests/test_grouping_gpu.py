@@ -1,0 +1,83 @@
+"""Device grouping must be bit-exact against the oracle's stable grouping."""
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = [
+    pytest.mark.gpu,
+    pytest.mark.skipif(not torch.cuda.is_available(), reason="CUDA device required"),
+]
+
+from oracle import cpu_reference as ref  # noqa: E402
+
+from loraforge_b200.ops.grouping import empty_routing, group_tokens  # noqa: E402
+
+
+def check(slots_np, num_slots, chunk):
+    slots = torch.tensor(slots_np, dtype=torch.int32, device="cuda")
+    routing = group_tokens(slots, num_slots, chunk=chunk)
+    torch.cuda.synchronize()
+    indptr, seg_slots, perm, count = ref.group_tokens(slots_np, num_slots, chunk)
+    got_count = int(routing.segment_count.item())
+    assert got_count == count
+    assert routing.segment_indptr[: count + 1].tolist() == indptr.tolist()
+    assert routing.segment_slots[:count].tolist() == seg_slots.tolist()
+    assert routing.token_indices[: len(slots_np)].tolist() == perm.tolist()
+
+
+@pytest.mark.parametrize("seed", range(4))
+@pytest.mark.parametrize("chunk", [0, 1, 16])
+def test_random_routing(seed, chunk):
+    rng = np.random.default_rng(seed)
+    num_slots = int(rng.integers(1, 300))
+    T = int(rng.integers(1, 3000))
+    check(rng.integers(-2, num_slots + 2, size=T), num_slots, chunk)
+
+
+@pytest.mark.parametrize(
+    "T,num_slots,chunk",
+    [(0, 4, 16), (1, 1, 16), (256, 128, 16), (512, 1024, 0), (8192, 64, 16), (40000, 16384, 16)],
+)
+def test_edge_sizes(T, num_slots, chunk):
+    rng = np.random.default_rng(T)
+    check(rng.integers(-1, num_slots, size=T), num_slots, chunk)
+
+
+def test_all_inactive_and_single_slot():
+    check(np.full(100, -1), 8, 16)
+    check(np.full(100, 3), 8, 16)
+    check(np.arange(100) % 2 - 1, 1, 0)
+
+
+def test_zipf_decode_batch_and_reuse_of_buffers():
+    rng = np.random.default_rng(7)
+    ranks = np.arange(1, 129)
+    p = 1.0 / ranks**1.1
+    slots = rng.choice(128, size=256, p=p / p.sum()).astype(np.int32)
+    out = empty_routing(256, "cuda")
+    for _ in range(2):
+        routing = group_tokens(torch.from_numpy(slots).cuda(), 128, chunk=16, out=out)
+        assert routing.segment_indptr.data_ptr() == out.segment_indptr.data_ptr()
+    indptr, seg_slots, perm, count = ref.group_tokens(slots, 128, 16)
+    assert out.segment_indptr[: count + 1].tolist() == indptr.tolist()
+    assert out.token_indices.tolist() == perm.tolist()
+
+
+def test_graph_capture_replays_with_new_routes():
+    slots = torch.zeros(300, dtype=torch.int32, device="cuda")
+    out = empty_routing(300, "cuda")
+    group_tokens(slots, 32, out=out)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        group_tokens(slots, 32, out=out)
+    rng = np.random.default_rng(3)
+    for _ in range(3):
+        new = rng.integers(-1, 32, size=300).astype(np.int32)
+        slots.copy_(torch.from_numpy(new))
+        graph.replay()
+        torch.cuda.synchronize()
+        indptr, seg_slots, perm, count = ref.group_tokens(new, 32, 16)
+        assert out.segment_count.item() == count
+        assert out.token_indices.tolist() == perm.tolist()
+        assert out.segment_slots[:count].tolist() == seg_slots.tolist()
