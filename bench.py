@@ -57,6 +57,7 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--seed", type=int, default=1234)
+    p.add_argument("--path", choices=("fused", "rows"), default="fused")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--profile", action="store_true", help="short run for ncu (no sampling/baselines)")
@@ -85,6 +86,7 @@ class Projection:
         self.scales = torch.full((N_SLOTS,), SCALE, dtype=torch.float32, device=device)
         self.slice_offsets = torch.tensor(np.cumsum((0, *widths)), dtype=torch.int32, device=device)
         self.z = torch.zeros(T_TOKENS, S * RANK, dtype=torch.bfloat16, device=device)
+        self.workspace = torch.empty(T_TOKENS, S * RANK, dtype=torch.float32, device=device)
         self.y = torch.zeros(T_TOKENS, N, dtype=torch.bfloat16, device=device)
 
     def b_rows(self, g):
@@ -92,11 +94,12 @@ class Projection:
         n = self.N * RANK
         return self.b_host[g * n : (g + 1) * n].view(self.N, RANK)
 
+    # Algorithmic bytes (the rank-r intermediate's round trip is not counted).
     def shrink_bytes(self, touched, t_active):
-        return t_active * self.K * 2 + touched * self.S * RANK * self.K * 2 + t_active * self.S * RANK * 2
+        return t_active * self.K * 2 + touched * self.S * RANK * self.K * 2
 
     def expand_bytes(self, touched, t_active):
-        return touched * self.N * RANK * 2 + t_active * self.N * 2 * 2 + t_active * self.S * RANK * 2
+        return touched * self.N * RANK * 2 + t_active * self.N * 2 * 2
 
     def flops(self, t_active):
         return t_active * 2 * RANK * (self.S * self.K + self.N)
@@ -134,28 +137,42 @@ class Workload:
 
 
 def run_step(w, events=None):
-    """Grouping + shrink/expand of the three projections through the public API."""
+    """Grouping + LoRA shrink/expand of the three projections through the public API.
+
+    ``w.path == "fused"``: one lora_shrink_expand launch per projection;
+    ``"rows"``: row_shrink + row_expand per projection (the reference's operator pair).
+    ``events[i]`` = (start, mid, end) CUDA events around projection i's launches.
+    """
     from loraforge_b200.ops import row_expand, row_shrink
+    from loraforge_b200.ops.fused import lora_shrink_expand
     from loraforge_b200.ops.grouping import group_tokens
 
     r = group_tokens(w.slots, N_SLOTS, chunk=16, out=w.routing)
+    routing = dict(
+        segment_indptr=r.segment_indptr, segment_slots=r.segment_slots,
+        token_indices=r.token_indices, segment_count=r.segment_count,
+    )
     for i, p in enumerate(w.projections):
+        meta = dict(b_offsets=p.b_offsets, b_strides=p.b_strides, ranks=p.ranks,
+                    scales=p.scales, slice_offsets=p.slice_offsets, **routing)
         if events is not None:
             events[i][0].record()
-        row_shrink(w.x_of(p), p.a, p.z, w.slots, p.ranks, num_slices=p.S, max_rank=RANK)
-        if events is not None:
-            events[i][1].record()
-        row_expand(
-            p.z, p.b, p.y, b_offsets=p.b_offsets, b_strides=p.b_strides, ranks=p.ranks,
-            scales=p.scales, segment_indptr=r.segment_indptr, segment_slots=r.segment_slots,
-            token_indices=r.token_indices, slice_offsets=p.slice_offsets,
-            segment_count=r.segment_count,
-        )
+        if w.path == "fused":
+            lora_shrink_expand(w.x_of(p), p.a, p.b, p.y, **meta, num_slices=p.S,
+                               workspace=p.workspace)
+            if events is not None:
+                events[i][1].record()
+        else:
+            row_shrink(w.x_of(p), p.a, p.z, w.slots, p.ranks, num_slices=p.S, max_rank=RANK)
+            if events is not None:
+                events[i][1].record()
+            row_expand(p.z, p.b, p.y, **meta)
         if events is not None:
             events[i][2].record()
 
 
-LAUNCHES_PER_STEP = 1 + 2 * len(PROJECTIONS)
+def launches_per_step(path):
+    return 1 + 2 * len(PROJECTIONS)  # grouping + two kernels per projection
 
 
 # ----------------------------------------------------------------------------- clocks
@@ -248,15 +265,8 @@ def time_graph(w, steps, warmup, flush):
     torch.cuda.current_stream().wait_stream(stream)
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in PROJECTIONS]
-    kernel_graphs = []
     with torch.cuda.graph(graph):
         run_step(w)
-    # Per-kernel timing uses a second graph with events between launches.
-    graph_ev = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph_ev):
-        run_step(w, events=ev)
-    kernel_graphs.append(graph_ev)
     for _ in range(warmup):
         flush.zero_()
         graph.replay()
@@ -270,16 +280,23 @@ def time_graph(w, steps, warmup, flush):
         ends[i].record()
     torch.cuda.synchronize()
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    # Kernel breakdown: shrink/expand time per projection, flushed before each step.
-    per_kernel = {f"{p[0]}.{k}": [] for p in PROJECTIONS for k in ("shrink", "expand")}
-    for _ in range(min(steps, 100)):
+    del graph
+    # Kernel breakdown: eager launches queued behind a device sleep so that host
+    # launch latency never shows up between the events; L2 flushed before each step.
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in PROJECTIONS]
+    kinds = ("fused",) if w.path == "fused" else ("shrink", "expand")
+    per_kernel = {f"{p[0]}.{k}": [] for p in PROJECTIONS for k in kinds}
+    for _ in range(min(steps, 50)):
         flush.zero_()
-        graph_ev.replay()
+        torch.cuda._sleep(4_000_000)
+        run_step(w, events=ev)
         torch.cuda.synchronize()
         for (name, _, _), (e0, e1, e2) in zip(PROJECTIONS, ev):
-            per_kernel[f"{name}.shrink"].append(e0.elapsed_time(e1))
-            per_kernel[f"{name}.expand"].append(e1.elapsed_time(e2))
-    del graph, kernel_graphs
+            if w.path == "fused":
+                per_kernel[f"{name}.fused"].append(e0.elapsed_time(e2))
+            else:
+                per_kernel[f"{name}.shrink"].append(e0.elapsed_time(e1))
+                per_kernel[f"{name}.expand"].append(e1.elapsed_time(e2))
     return step_ms, {k: statistics.mean(v) for k, v in per_kernel.items()}
 
 
@@ -411,6 +428,7 @@ def main():
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     w = Workload(device, args.seed + rank)
+    w.path = args.path
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
     steps, warmup = args.steps, max(3, args.warmup)
     barrier(world)
@@ -424,7 +442,11 @@ def main():
     dominant = max(per_kernel, key=per_kernel.get)
     name, kind = dominant.split(".")
     p = next(p for p in w.projections if p.name == name)
-    alg = (p.shrink_bytes if kind == "shrink" else p.expand_bytes)(w.touched, w.t_active)
+    alg = {
+        "shrink": p.shrink_bytes(w.touched, w.t_active),
+        "expand": p.expand_bytes(w.touched, w.t_active),
+        "fused": p.shrink_bytes(w.touched, w.t_active) + p.expand_bytes(w.touched, w.t_active),
+    }[kind]
     achieved = alg / (per_kernel[dominant] * 1e-3) / 1e9
     result = {
         "metric": "multi-LoRA shrink+expand tokens/s (decode, config 1)",
@@ -439,7 +461,7 @@ def main():
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded; BASELINE config 1 shapes and distributions)",
-        "config": config | {"parallelism": f"replicas{world}"},
+        "config": config | {"parallelism": f"replicas{world}", "path": w.path},
         "hbm_gbs_step": w.bytes_per_step() / (ms_per_step * 1e-3) / 1e9,
         "bytes_per_step": w.bytes_per_step(),
         "flops_per_step": w.flops_per_step(),
@@ -454,7 +476,7 @@ def main():
             "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
             "traffic": None,
         },
-        "gpu_launches": LAUNCHES_PER_STEP * steps,
+        "gpu_launches": launches_per_step(w.path) * steps,
         "clocks": clocks.record(),
     }
     if not args.no_e2e and not args.profile:

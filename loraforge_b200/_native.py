@@ -48,6 +48,10 @@ SIGNATURES = {
     ],
     "lf_vllm_shrink": [_i32, _p, _i64, _p, _i32, _i32, _p, _p, _i64, _i64, _i32, _f32, _p],
     "lf_vllm_expand": [_i32, _p, _p, _i32, _i32, _p, _i64, _p, _i64, _i32, _i64, _i32, _p],
+    "lf_fused_shrink_expand": [
+        _p, _i64, _p, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _i64,
+        _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _p,
+    ],
 }
 
 _lock = threading.Lock()

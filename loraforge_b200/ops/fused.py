@@ -1,0 +1,150 @@
+"""Fused retained-rank shrink -> expand for decode segments (one launch, z on chip).
+
+``lora_shrink_expand`` takes the operands of ``row_shrink`` (x, packed A) and of
+``row_expand`` (compact B store, per-slot metadata, routing tables) and computes
+``output += scale * B @ (A @ x)`` for every routed token in one call: a grouped
+shrink kernel (each adapter's A rows read once per segment, K split over a
+thread-block cluster) chained by programmatic dependent launch to a grouped expand
+kernel, with the rank-r intermediate kept in FP32.  It is the B200 form of the reference's two-kernel decode
+path (src/loraforge/ops/lora_rows.py:54-239 as driven by
+src/loraforge/integrations/_sglang_fleet.py:271-407).
+
+``numerics="fp32"`` (default) keeps z in FP32 and rounds the output once;
+``numerics="reference"`` reproduces the retained-rank operators' contract (BF16 z,
+BF16-rounded scaled delta, BF16 sum), so it agrees with ``row_shrink`` followed by
+``row_expand`` up to the FP32 summation order of the shrink.
+"""
+
+from __future__ import annotations
+
+from loraforge_b200 import _native
+from loraforge_b200.annotations import ExperimentalAPI
+from loraforge_b200.ops.lora_rows import _distinct_output, _tensor, _vector
+
+NUMERICS = {"fp32": 0, "reference": 1}
+
+
+@ExperimentalAPI(reason="Fused BF16 decode shrink/expand; sm_100a tensor cores, caller-owned metadata.")
+def lora_shrink_expand(
+    x,
+    a,
+    b,
+    output,
+    *,
+    b_offsets,
+    b_strides,
+    ranks,
+    scales,
+    segment_indptr,
+    segment_slots,
+    token_indices,
+    slice_offsets,
+    segment_count,
+    num_slices: int = 1,
+    numerics: str = "fp32",
+    workspace=None,
+) -> None:
+    """Add ``scale * B_g @ (A_g @ x[t])`` to ``output[t]`` for every routed token.
+
+    x [tokens, width]; A [slots, slices*capacity, width]; output [tokens, N] with
+    slice_offsets partitioning N; B flat with b_offsets (8-element aligned) and
+    power-of-two b_strides in 1..64; segments of at most 16 tokens, one slot each
+    (``group_tokens(..., chunk=16)``).  Slot -1 / rank-0 segments leave output
+    unchanged.  ``workspace`` is an optional FP32 [tokens, slices*capacity] buffer
+    for the intermediate (allocated per call when omitted; pass one to keep a
+    captured graph allocation-free).
+    """
+    import torch
+
+    _tensor(x, "x", 2, torch.bfloat16)
+    _tensor(a, "a", 3, torch.bfloat16, x.device)
+    _tensor(b, "b", 1, torch.bfloat16, x.device)
+    _tensor(output, "output", 2, torch.bfloat16, x.device)
+    if type(num_slices) is not int or not 1 <= num_slices <= 4:
+        raise ValueError("num_slices must be in 1..4")
+    if numerics not in NUMERICS:
+        raise ValueError("numerics must be 'fp32' or 'reference'")
+    _vector(ranks, "ranks", torch.int32, x.device, a.shape[0])
+    nslots = ranks.numel()
+    for tensor, name, dtype in (
+        (b_offsets, "b_offsets", torch.int64),
+        (b_strides, "b_strides", torch.int32),
+        (scales, "scales", torch.float32),
+    ):
+        _vector(tensor, name, dtype, x.device, nslots)
+    _vector(segment_slots, "segment_slots", torch.int32, x.device)
+    _vector(segment_indptr, "segment_indptr", torch.int32, x.device, segment_slots.numel() + 1)
+    _vector(token_indices, "token_indices", torch.int32, x.device)
+    _vector(slice_offsets, "slice_offsets", torch.int32, x.device, num_slices + 1)
+    _vector(segment_count, "segment_count", torch.int32, x.device, 1)
+    if (
+        a.shape[1] % num_slices
+        or a.shape[2] != x.shape[1]
+        or output.shape[0] != x.shape[0]
+        or output.shape[1] < 1
+    ):
+        raise ValueError("A/output shapes must agree with slices and tokens")
+    if (
+        x.shape[1] % 8
+        or x.stride(1) != 1
+        or x.stride(0) % 8
+        or x.stride(0) < x.shape[1]
+        or x.data_ptr() % 16
+        or not a.is_contiguous()
+        or a.data_ptr() % 16
+        or not b.is_contiguous()
+        or b.data_ptr() % 16
+    ):
+        raise ValueError("expected aligned A/B/x with width and row stride multiples of 8")
+    if output.stride(1) != 1 or output.stride(0) % 4 or output.stride(0) < output.shape[1] or output.data_ptr() % 8:
+        raise ValueError("output rows must be 8-byte aligned with a row stride multiple of 4")
+    _distinct_output(
+        output,
+        (x, a, b, b_offsets, b_strides, ranks, scales, segment_indptr, segment_slots,
+         token_indices, slice_offsets, segment_count),
+    )
+    capacity = a.shape[1] // num_slices
+    if workspace is None:
+        workspace = torch.empty(x.shape[0], num_slices * capacity, dtype=torch.float32, device=x.device)
+    if (
+        not isinstance(workspace, torch.Tensor)
+        or workspace.dtype != torch.float32
+        or workspace.device != x.device
+        or workspace.ndim != 2
+        or workspace.shape[0] < x.shape[0]
+        or workspace.shape[1] < num_slices * capacity
+        or workspace.stride(1) != 1
+    ):
+        raise ValueError("workspace must be FP32 [tokens, slices*capacity] on the same device")
+    if x.shape[0] == 0:
+        return
+    with torch.cuda.device(x.device):
+        _native.call(
+            "lf_fused_shrink_expand",
+            x.data_ptr(),
+            x.stride(0),
+            a.data_ptr(),
+            b.data_ptr(),
+            b_offsets.data_ptr(),
+            b_strides.data_ptr(),
+            output.data_ptr(),
+            output.stride(0),
+            segment_indptr.data_ptr(),
+            segment_slots.data_ptr(),
+            token_indices.data_ptr(),
+            ranks.data_ptr(),
+            scales.data_ptr(),
+            slice_offsets.data_ptr(),
+            segment_count.data_ptr(),
+            workspace.data_ptr(),
+            workspace.stride(0),
+            x.shape[0],
+            x.shape[1],
+            output.shape[1],
+            num_slices,
+            capacity,
+            nslots,
+            segment_slots.numel(),
+            NUMERICS[numerics],
+            _native.stream_of(x.device),
+        )

@@ -261,3 +261,28 @@ def lora_delta_fp32(x, a, b_rows, slots, ranks, scales, slice_offsets, threads=N
                 "tr,nr->tn", zz[:, s * r : (s + 1) * r], B[lo:hi]
             )
     return out.numpy()
+
+
+# ----------------------------------------------------------------------------- gates
+def half_ulp_bf16(values) -> np.ndarray:
+    """Half a BF16 unit in the last place of each value (the rounding of an exact value)."""
+    v = np.abs(np.asarray(values, dtype=np.float64))
+    _, e = np.frexp(v)  # v = m * 2**e, m in [0.5, 1)
+    return np.where(v > 0, np.ldexp(1.0, e - 9), 0.0)
+
+
+def fp32_gate(out_values, ref32) -> dict:
+    """BASELINE's max-abs gate for a BF16 output against the FP32 einsum.
+
+    ``raw``: max|out - ref| / RMS(ref) (>= the output rounding itself, ~0.015 for
+    Gaussian outputs); ``excess``: the same after discounting the half-ulp rounding
+    that any BF16 output must incur — this is the number compared with 1e-2;
+    ``exact``: the fraction of outputs equal to bf16(ref).
+    """
+    out = np.asarray(out_values, dtype=np.float64)
+    ref = np.asarray(ref32, dtype=np.float64)
+    rms = float(np.sqrt(np.mean(ref * ref))) or 1.0
+    err = np.abs(out - ref)
+    excess = np.maximum(err - half_ulp_bf16(ref), 0.0)
+    exact = float(np.mean(round_bf16(ref.astype(F32)) == out.astype(F32)))
+    return {"raw": float(err.max()) / rms, "excess": float(excess.max()) / rms, "exact": exact}
