@@ -178,6 +178,14 @@ int lf_fused_shrink_expand(const void* x, int64_t x_stride, const void* a, const
                            int32_t capacity, int32_t num_slots, int32_t max_segments,
                            int32_t numerics, void* stream);
 
+/*
+ * Number of bounded device-side waits (mbarrier polls in the bulk-copy kernels)
+ * that expired since the last reset; a non-zero count means a kernel gave up and
+ * skipped work instead of hanging.  Synchronous; reset != 0 clears the counter.
+ * No reference counterpart (the reference kernels have no waits).
+ */
+int lf_device_wait_timeouts(int32_t* count, int32_t reset);
+
 #ifdef __cplusplus
 }
 #endif

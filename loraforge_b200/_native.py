@@ -52,6 +52,7 @@ SIGNATURES = {
         _p, _i64, _p, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _i64,
         _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _p,
     ],
+    "lf_device_wait_timeouts": [_p, _i32],
 }
 
 _lock = threading.Lock()
@@ -95,6 +96,13 @@ def call(name: str, *args) -> None:
     if status != 0:
         message = lib.lf_last_error_string().decode(errors="replace")
         raise RuntimeError(message or f"{name} failed with status {status}")
+
+
+def device_wait_timeouts(reset: bool = False) -> int:
+    """Expired bounded device waits since the last reset (synchronous)."""
+    count = ctypes.c_int32(0)
+    call("lf_device_wait_timeouts", ctypes.byref(count), 1 if reset else 0)
+    return count.value
 
 
 def stream_of(device) -> int:

@@ -206,9 +206,9 @@ int launch_bgmv_expand(const void* z, const void* b, const void* ranks, const vo
   using St = typename T::storage;
   const dim3 grid(unsigned(T_tokens), unsigned((N + 255) / 256));
   const size_t smem = sizeof(float) * size_t(S) * rmax;
-  static unsigned long long flags = 0;
+  static int flags[64] = {};
   auto kernel = bgmv_expand_kernel<T, I, OI, SC>;
-  if (int rc = ensure_smem(kernel, int(smem), &flags)) return rc;
+  if (int rc = ensure_smem(kernel, int(smem), flags)) return rc;
   kernel<<<grid, 256, smem, stream>>>(static_cast<const St*>(z), static_cast<const St*>(b),
                                       ranks, static_cast<const typename SC::storage*>(scales),
                                       map, offsets, static_cast<St*>(y), ys0, ys1, N, num_slots,

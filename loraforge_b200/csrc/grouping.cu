@@ -170,8 +170,8 @@ extern "C" int lf_group_tokens(const int32_t* slots, int64_t num_tokens, int32_t
   if (fixed > limit) return fail(LF_E_INVALID, "group_tokens: too many slots");
   const int cache = fixed + sizeof(int) * size_t(T) <= limit ? 1 : 0;
   const size_t bytes = fixed + (cache ? sizeof(int) * size_t(T) : 0);
-  static unsigned long long flags = 0;
-  if (int rc = ensure_smem(group_tokens_kernel, int(limit), &flags)) return rc;
+  static int flags[64] = {};
+  if (int rc = ensure_smem(group_tokens_kernel, int(limit), flags)) return rc;
   group_tokens_kernel<<<1, kGroupThreads, bytes, static_cast<cudaStream_t>(stream)>>>(
       slots, T, num_slots, chunk, segment_indptr, segment_slots, token_indices,
       segment_count, cache);

@@ -5,19 +5,20 @@
 
 namespace lfb {
 
-// Raise a kernel's dynamic shared-memory limit once per device.  `flags` is a
-// per-kernel bitmask of devices already configured (devices 0..63).
+// Raise a kernel's dynamic shared-memory limit on the current device when `bytes`
+// exceeds what was configured there before.  `configured` holds one entry per device
+// (devices 0..63) for this kernel.
 template <typename Kernel>
-inline int ensure_smem(Kernel kernel, int bytes, unsigned long long* flags) {
+inline int ensure_smem(Kernel kernel, int bytes, int* configured) {
   if (bytes <= 48 * 1024) return LF_OK;
   int device = 0;
   if (cudaGetDevice(&device) != cudaSuccess) return check_launch("cudaGetDevice");
-  const unsigned long long bit = 1ull << (device & 63);
-  if (*flags & bit) return LF_OK;
+  int& have = configured[device & 63];
+  if (have >= bytes) return LF_OK;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) !=
       cudaSuccess)
     return check_launch("cudaFuncSetAttribute");
-  *flags |= bit;
+  have = bytes;
   return LF_OK;
 }
 

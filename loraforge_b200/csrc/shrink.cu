@@ -325,9 +325,9 @@ template <typename T, int VEC, typename L>
 int launch_shrink(const L& layout, const typename T::storage* x, int64_t x_stride,
                   int64_t T_tokens, int64_t K, int num_slots, int max_rows,
                   cudaStream_t stream, const char* what) {
-  static unsigned long long flags = 0;
+  static int flags[64] = {};
   auto kernel = slot_shrink_kernel<T, VEC, L>;
-  if (int rc = ensure_smem(kernel, int(kShrinkSmem), &flags)) return rc;
+  if (int rc = ensure_smem(kernel, int(kShrinkSmem), flags)) return rc;
   const int row_blocks = (max_rows + kRowsPerCta - 1) / kRowsPerCta;
   if (row_blocks < 1 || row_blocks > 65535) return fail(LF_E_INVALID, "shrink: too many rank rows");
   const int parts = k_parts(K);

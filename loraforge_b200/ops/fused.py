@@ -1,4 +1,4 @@
-"""Fused retained-rank shrink -> expand for decode segments (one launch, z on chip).
+"""Grouped retained-rank shrink -> expand for decode segments (SGMV, z kept in FP32).
 
 ``lora_shrink_expand`` takes the operands of ``row_shrink`` (x, packed A) and of
 ``row_expand`` (compact B store, per-slot metadata, routing tables) and computes

@@ -168,3 +168,12 @@ def test_rejects_unaligned_output_and_empty_batch():
     with pytest.raises(ValueError, match="8-byte"):
         lora_shrink_expand(x, a, b, base[:, 1:], **meta, num_slices=S)
     lora_shrink_expand(x[:0], a, b, base[:0], **meta, num_slices=S)
+
+
+def test_no_device_wait_expired():
+    # Every bounded mbarrier wait in the bulk-copy kernels completed in time.
+    from loraforge_b200 import _native
+
+    x, a, b, base, slots_t, meta, S, cap = decode_case(seed=9, widths=(14336, 14336))
+    fused(x, a, b, base.clone(), meta, S)
+    assert _native.device_wait_timeouts(reset=True) == 0
