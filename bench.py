@@ -86,7 +86,11 @@ class Projection:
         self.scales = torch.full((N_SLOTS,), SCALE, dtype=torch.float32, device=device)
         self.slice_offsets = torch.tensor(np.cumsum((0, *widths)), dtype=torch.int32, device=device)
         self.z = torch.zeros(T_TOKENS, S * RANK, dtype=torch.bfloat16, device=device)
-        self.workspace = torch.empty(T_TOKENS, S * RANK, dtype=torch.float32, device=device)
+        from loraforge_b200.ops.fused import workspace_floats
+
+        self.workspace = torch.empty(
+            workspace_floats(T_TOKENS, K, S, RANK), dtype=torch.float32, device=device
+        )
         self.y = torch.zeros(T_TOKENS, N, dtype=torch.bfloat16, device=device)
 
     def b_rows(self, g):

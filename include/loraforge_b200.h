@@ -156,12 +156,12 @@ int lf_vllm_expand(int32_t dtype, const float* v, const lf_slice_desc* slices,
  * (compact B, b_offsets/b_strides, routing tables, scales, slice_offsets) in one
  * call of two chained kernels.  For every active segment (slot g, rank r in 1..64,
  * bucket b) and output column n of slice s:
- *   z[t, j] = sum_i x[t, i] * A[g, j, i]            (j < S*r, FP32 into `workspace`)
+ *   z[t, j] = sum_i x[t, i] * A[g, j, i]            (j < S*r, FP32)
  *   numerics 0 (fp32):      y[t, n] = bf16(y + scale_g * sum_k z[t, s*r+k] B_g[n, k])
  *   numerics 1 (reference): y[t, n] = bf16(y + bf16(scale_g * sum_k bf16(z) B_g[n, k]))
- * with k < min(r, b).  `workspace` is FP32 scratch with row t at
- * workspace + t*workspace_stride (workspace_stride >= S*capacity); rows of routed
- * tokens are overwritten.  Deterministic (fixed-order reductions, no atomics).
+ * with k < min(r, b).  `workspace` is FP32 scratch of at least
+ * lf_fused_workspace_floats(...) floats, 16-byte aligned, holding per-K-chunk
+ * partial sums of z (added in chunk order, so results are deterministic; no atomics).
  * Requires width and x_stride multiples of 8, 16-byte aligned x/A/B, 8-byte aligned
  * y with y_stride a multiple of 4 and B regions at 8-element offsets.  Fused,
  * grouped form of the reference's two decode kernels (src/loraforge/ops/csrc/
@@ -173,10 +173,14 @@ int lf_fused_shrink_expand(const void* x, int64_t x_stride, const void* a, const
                            const int32_t* segment_slots, const int32_t* token_indices,
                            const int32_t* ranks, const float* scales,
                            const int32_t* slice_offsets, const int32_t* segment_count,
-                           float* workspace, int64_t workspace_stride, int64_t num_tokens,
+                           float* workspace, int64_t workspace_floats, int64_t num_tokens,
                            int64_t width, int32_t out_width, int32_t num_slices,
                            int32_t capacity, int32_t num_slots, int32_t max_segments,
                            int32_t numerics, void* stream);
+
+/* Workspace floats lf_fused_shrink_expand needs for these sizes (-1 if invalid). */
+int64_t lf_fused_workspace_floats(int64_t num_tokens, int64_t width, int32_t num_slices,
+                                  int32_t capacity);
 
 /*
  * Number of bounded device-side waits (mbarrier polls in the bulk-copy kernels)

@@ -61,7 +61,7 @@ _lib = None
 
 def exported_symbols() -> tuple[str, ...]:
     """Every symbol the header declares (checked by the CPU test suite)."""
-    return ("lf_version", "lf_last_error_string", *SIGNATURES)
+    return ("lf_version", "lf_last_error_string", "lf_fused_workspace_floats", *SIGNATURES)
 
 
 def library() -> ctypes.CDLL:
@@ -85,6 +85,8 @@ def library() -> ctypes.CDLL:
                 fn = getattr(lib, name)
                 fn.restype = ctypes.c_int
                 fn.argtypes = args
+            lib.lf_fused_workspace_floats.restype = ctypes.c_int64
+            lib.lf_fused_workspace_floats.argtypes = [_i64, _i64, _i32, _i32]
             _lib = lib
     return _lib
 
@@ -96,6 +98,14 @@ def call(name: str, *args) -> None:
     if status != 0:
         message = lib.lf_last_error_string().decode(errors="replace")
         raise RuntimeError(message or f"{name} failed with status {status}")
+
+
+def fused_workspace_floats(num_tokens: int, width: int, num_slices: int, capacity: int) -> int:
+    """FP32 workspace size of lf_fused_shrink_expand for these sizes."""
+    n = library().lf_fused_workspace_floats(num_tokens, width, num_slices, capacity)
+    if n < 0:
+        raise ValueError("invalid sizes for the fused workspace")
+    return n
 
 
 def device_wait_timeouts(reset: bool = False) -> int:

@@ -1,40 +1,37 @@
-// Grouped (SGMV) LoRA shrink -> expand for decode segments of <= 16 tokens (one slot each).
+// Grouped (SGMV) LoRA shrink -> expand over decode segments of <= 16 tokens (one slot each).
 //
 // Two streaming kernels per call, chained with programmatic dependent launch:
 //
-//   sgmv_shrink_kernel   z[t, j] = sum_k x[t, k] * A_g[j, k]  (j < S*r), FP32, for every
-//                        token t of a segment.  Grid = (K part, segment); the K parts of a
-//                        segment form one thread-block cluster and their partial [16 x S*r]
-//                        tiles are summed in a fixed rank order through distributed shared
-//                        memory by rank 0, which writes z to the FP32 workspace.  Every A
-//                        row is read from HBM once per segment; no atomics.
-//   sgmv_expand_kernel   y[t, n] += scale_g * sum_k z[t, slice(n)*r + k] * B_g[n, k] for a
-//                        (column chunk, segment) tile; z is read back from the workspace.
+//   sgmv_shrink_kernel   partial z[c][t, j] = sum_{k in chunk c} x[t, k] * A_g[j, k] for
+//                        every token t of a segment and j < S*r.  Persistent CTAs walk a
+//                        contiguous range of (segment, K chunk) units; each unit's x rows
+//                        and A rows are staged in shared memory by a 3-deep cp.async
+//                        pipeline, so every A row is read from HBM once per segment.  The
+//                        FP32 partials go to the workspace; no atomics.
+//   sgmv_expand_*        y[t, n] += scale_g * sum_k z[t, slice(n)*r + k] * B_g[n, k], with
+//                        z = sum over chunks of the partials, added in chunk order (so
+//                        results are deterministic).  The bulk-copy kernel streams B rows
+//                        and y rows through a shared-memory ring with cp.async.bulk; the
+//                        direct kernel (outputs that are not 16-byte aligned) reads them
+//                        with vector loads.
 //
-// Both run on the tensor cores (mma.sync m16n8k16 / m16n8k8, BF16 operands, FP32
-// accumulate) with the segment's tokens as the M dimension.  Fragments are loaded
-// straight from global memory with 16-byte vector loads: inside each 32-element K
-// block the MMA fragment slots carry a permutation of k that is the same for both
-// operands, so a lane's 16 contiguous bytes feed two MMAs with no shared-memory
-// staging.  Output columns are permuted the same way so that each lane owns four
-// consecutive outputs (8-byte read-modify-write of y).
+// The MMAs run on the tensor cores (mma.sync m16n8k16 / m16n8k8, BF16 operands, FP32
+// accumulate) with the segment's tokens as the M dimension.  Inside each 32-element K
+// block the fragment slots carry a permutation of k that is the same for both
+// operands, so a lane's 16 contiguous bytes feed two MMAs.  Output columns are
+// permuted the same way so that each lane owns four consecutive outputs.
 //
 // Numerics: kFp32 keeps z in FP32 (split into BF16 hi + lo for the expand MMAs, about
 // 16 significant bits) and rounds the output once: y = bf16(y + scale*acc).
 // kReference reproduces the retained-rank operators' contract: z rounded to BF16,
 // delta = bf16(acc*scale), y = bf16(y + delta)
 // (src/loraforge/ops/csrc/lora_rows.cu:64 and :113).
-#include <cooperative_groups.h>
-
 #include "launch.cuh"
 #include "tma.cuh"
-
-namespace cg = cooperative_groups;
 
 namespace lfb {
 namespace {
 
-constexpr int kMaxCluster = 16;  // non-portable cluster size on sm_100
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kSeg = 16;          // tokens per segment (one m16 tile)
@@ -66,11 +63,27 @@ struct FusedParams {
   const float* scales;
   const int32_t* slice_offsets;
   const int32_t* seg_count;
-  float* z;          // FP32 workspace, row t at z + t * z_stride
-  int64_t z_stride;  // >= S * cap
+  float* z;                // FP32 workspace: partial c of token t at z + c*z_chunk + t*z_stride
+  int64_t z_stride;        // >= S * cap, a multiple of 4
+  int64_t z_chunk;         // floats per chunk partial (T * z_stride)
   int T, K, N, S, cap, num_slots, max_segments;
-  int units_per_chunk;  // expand: 16-column units per CTA
+  int nchunks;             // K chunks of the shrink (partials to add per z value)
+  int units_per_chunk;     // direct expand: 16-column units per CTA
 };
+
+// Sum of the shrink's chunk partials for token `tok`, packed column `j`.
+__device__ __forceinline__ float z_value(const FusedParams& p, int tok, int j) {
+  const float* zp = p.z + int64_t(tok) * p.z_stride + j;
+  float sum = 0.f;
+  for (int c = 0; c < p.nchunks; ++c) sum += zp[c * p.z_chunk];
+  return sum;
+}
+
+__device__ __forceinline__ uint32_t cvt_bf16x2(float first, float second) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(second), "f"(first));
+  return r;
+}
 
 // ------------------------------------------------------------------ tensor-core helpers
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
@@ -363,150 +376,205 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 }
 
 // ------------------------------------------------------------------ shrink kernel
-// grid (cluster_k, max_segments), cluster (cluster_k, 1, 1).  Each CTA stages its
-// K slice of the segment's x rows (slots 0..15) and A rows (slots 16..) in shared
-// memory with one burst of 16-byte cp.async copies (row pitch = kslice*2 + 64 bytes,
-// so the fragment loads below are free of bank conflicts), then runs the MMAs from
-// shared memory.  After the MMAs the tile region is reused for the partial sums.
+constexpr int kShrinkStages = 3;
+
+struct alignas(16) ShrinkHeader {
+  int ok, chunk, n, g, r;
+  int pad[3];
+  int tok[kSeg];
+};
+
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
                : "memory");
 }
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.commit_group;\n cp.async.wait_group 0;" ::: "memory");
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 __device__ __forceinline__ uint4 lds16(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
 
-__global__ void __launch_bounds__(kThreads, 3)
-sgmv_shrink_kernel(const __grid_constant__ FusedParams p, int kslice) {
-  extern __shared__ __align__(128) uint8_t tiles[];
-  __shared__ int tok[kSeg];
+// Persistent grid over (segment, K chunk) units, segment-major, a contiguous range
+// per CTA.  A stage holds one unit: x rows of the segment's tokens in slots 0..15 and
+// the slot's S*r A rows from slot 16, each `kc` columns wide with a row pitch of
+// kc*2 + 64 bytes (kc a multiple of 64, so the 16-byte fragment loads below hit
+// distinct bank groups).
+__global__ void __launch_bounds__(kThreads, 2)
+sgmv_shrink_kernel(const __grid_constant__ FusedParams p, int kc, int stage_bytes) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  ShrinkHeader* hdr = reinterpret_cast<ShrinkHeader*>(smem + kShrinkStages * stage_bytes);
+  float* warp_part = reinterpret_cast<float*>(hdr + kShrinkStages);  // [kparts][16][8*ntiles]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g8 = lane >> 2, t4 = lane & 3;
-  const int parts = gridDim.x, rank = blockIdx.x;
-  SegmentInfo si;
-  int start = 0;
-  // Every CTA of a cluster shares the segment, so these exits are cluster-uniform.
-  if (!load_segment(p, blockIdx.y, si, start) || !load_tokens(p, si, start, tok)) {
-    pdl_launch_dependents();
-    return;
-  }
-  const int kb = min(p.K, rank * kslice);
-  const int klen = min(p.K, kb + kslice) - kb;  // a multiple of 8
-  const int pitch = kslice * 2 + 64;
-  const int R = p.S * si.r;
-  // ---- stage x rows (m < n) and A rows (j < R) of this K slice
-  const int chunks = klen / 8;
-  const int rows = si.n + R;
-  for (int idx = tid; idx < rows * chunks; idx += kThreads) {
-    const int row = idx / chunks, c = idx - row * chunks;
-    const uint16_t* src;
-    int slot;
-    if (row < si.n) {
-      src = p.x + int64_t(tok[row]) * p.x_stride + kb + c * 8;
-      slot = row;
-    } else {
-      const int j = row - si.n;
-      src = p.a + (int64_t(si.g) * p.S * p.cap + j) * p.K + kb + c * 8;
-      slot = kSeg + j;
+  const int pitch = kc * 2 + 64;
+  const int nseg = min(*p.seg_count, p.max_segments);
+  const int nunits = nseg * p.nchunks;
+  const int per = (nunits + gridDim.x - 1) / gridDim.x;
+  const int u0 = min(nunits, int(blockIdx.x) * per);
+  const int u1 = min(nunits, u0 + per);
+  // Warp 0 keeps the metadata of the segment it described last.
+  int cseg = -1, cstart = 0, ctok = -1;
+  bool cok = false;
+  SegmentInfo csi{};
+
+  // Describe unit u in stage st and start its copies (one cp.async group per call).
+  auto issue = [&](int u, int st) {
+    if (warp == 0 && u < u1) {
+      const int seg = u / p.nchunks;
+      if (seg != cseg) {
+        cseg = seg;
+        cok = load_segment(p, seg, csi, cstart);
+        ctok = (cok && lane < csi.n) ? p.perm[cstart + lane] : -1;
+        const bool bad = cok && lane < csi.n && (ctok < 0 || ctok >= p.T);
+        cok = cok && !__any_sync(0xffffffffu, bad);
+      }
+      if (lane < kSeg) hdr[st].tok[lane] = ctok;
+      if (lane == 0) {
+        hdr[st].ok = cok ? 1 : 0;
+        hdr[st].chunk = u - seg * p.nchunks;
+        hdr[st].n = csi.n;
+        hdr[st].g = csi.g;
+        hdr[st].r = csi.r;
+      }
     }
-    cp_async16(tiles + slot * pitch + c * 16, src);
-  }
-  cp_async_wait_all();
-  __syncthreads();
-  // ---- MMAs: warps own 8-row tiles of A (and split K when there are few tiles)
-  const int ntiles = (R + 7) / 8;
-  const int kparts = ntiles >= kWarps ? 1 : kWarps / ntiles;
-  const int my_tile0 = ntiles >= kWarps ? warp : warp % ntiles;
-  const int my_kpart = ntiles >= kWarps ? 0 : warp / ntiles;
-  const bool active = my_kpart < kparts;
-  float acc[kMaxTilesPerWarp][4];
+    __syncthreads();
+    if (u < u1 && hdr[st].ok) {
+      const ShrinkHeader& h = hdr[st];
+      const int kb = h.chunk * kc;
+      const int c16 = (min(p.K, kb + kc) - kb) / 8;
+      const int rows = h.n + p.S * h.r;
+      uint8_t* base = smem + st * stage_bytes;
+      for (int idx = tid; idx < rows * c16; idx += kThreads) {
+        const int row = idx / c16, c = idx - row * c16;
+        const uint16_t* src;
+        int slot;
+        if (row < h.n) {
+          src = p.x + int64_t(h.tok[row]) * p.x_stride + kb + c * 8;
+          slot = row;
+        } else {
+          const int j = row - h.n;
+          src = p.a + (int64_t(h.g) * p.S * p.cap + j) * p.K + kb + c * 8;
+          slot = kSeg + j;
+        }
+        cp_async16(base + slot * pitch + c * 16, src);
+      }
+    }
+    cp_async_commit();
+  };
+
+  issue(u0, 0);
+  issue(u0 + 1, 1);
+  for (int u = u0, k = 0; u < u1; ++u, ++k) {
+    const int st = k % kShrinkStages;
+    issue(u + 2, (k + 2) % kShrinkStages);
+    cp_async_wait<2>();  // unit u's group has landed
+    __syncthreads();
+    const ShrinkHeader& h = hdr[st];
+    if (h.ok) {
+      const uint8_t* base = smem + st * stage_bytes;
+      const int klen = min(p.K, (h.chunk + 1) * kc) - h.chunk * kc;
+      const int R = p.S * h.r;
+      const int ntiles = (R + 7) / 8;
+      const int kparts = ntiles >= kWarps ? 1 : kWarps / ntiles;
+      const int my_tile0 = ntiles >= kWarps ? warp : warp % ntiles;
+      const int my_kpart = ntiles >= kWarps ? 0 : warp / ntiles;
+      const bool active = my_kpart < kparts;
+      float acc[kMaxTilesPerWarp][4];
 #pragma unroll
-  for (int i = 0; i < kMaxTilesPerWarp; ++i)
+      for (int i = 0; i < kMaxTilesPerWarp; ++i)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) acc[i][e] = 0.f;
-  if (active) {
-    const int kblocks = (klen + 31) / 32;
-    const int b0 = kblocks * my_kpart / kparts, b1 = kblocks * (my_kpart + 1) / kparts;
-    const uint8_t* xr0 = tiles + g8 * pitch;
-    const uint8_t* xr1 = tiles + (g8 + 8) * pitch;
-    const uint4 zero = make_uint4(0, 0, 0, 0);
+        for (int e = 0; e < 4; ++e) acc[i][e] = 0.f;
+      if (active) {
+        const int kblocks = (klen + 31) / 32;
+        const int b0 = kblocks * my_kpart / kparts, b1 = kblocks * (my_kpart + 1) / kparts;
+        const uint8_t* xr0 = base + g8 * pitch;
+        const uint8_t* xr1 = base + (g8 + 8) * pitch;
+        const uint4 zero = make_uint4(0, 0, 0, 0);
 #pragma unroll 4
-    for (int b = b0; b < b1; ++b) {
-      const int k = b * 32 + 8 * t4;
-      const bool kin = k < klen;
-      const uint4 x0 = kin ? lds16(xr0 + k * 2) : zero;
-      const uint4 x1 = kin ? lds16(xr1 + k * 2) : zero;
+        for (int blk = b0; blk < b1; ++blk) {
+          const int kk = blk * 32 + 8 * t4;
+          const bool kin = kk < klen;
+          const uint4 x0 = kin ? lds16(xr0 + kk * 2) : zero;
+          const uint4 x1 = kin ? lds16(xr1 + kk * 2) : zero;
 #pragma unroll
-      for (int i = 0; i < kMaxTilesPerWarp; ++i) {
-        const int tile = my_tile0 + i * kWarps;
-        if (tile < ntiles) {
-          const uint4 av = kin ? lds16(tiles + (kSeg + tile * 8 + g8) * pitch + k * 2) : zero;
-          mma16816(acc[i], x0.x, x1.x, x0.y, x1.y, av.x, av.y);
-          mma16816(acc[i], x0.z, x1.z, x0.w, x1.w, av.z, av.w);
+          for (int i = 0; i < kMaxTilesPerWarp; ++i) {
+            const int tile = my_tile0 + i * kWarps;
+            if (tile < ntiles) {
+              const uint4 av = kin ? lds16(base + (kSeg + tile * 8 + g8) * pitch + kk * 2) : zero;
+              mma16816(acc[i], x0.x, x1.x, x0.y, x1.y, av.x, av.y);
+              mma16816(acc[i], x0.z, x1.z, x0.w, x1.w, av.z, av.w);
+            }
+          }
+        }
+      }
+      float* zc = p.z + int64_t(h.chunk) * p.z_chunk;
+      if (kparts == 1) {
+        // Warps beyond ntiles hold no tile.  Rows m >= n belong to no token.
+        if (active) {
+#pragma unroll
+          for (int i = 0; i < kMaxTilesPerWarp; ++i) {
+            const int tile = my_tile0 + i * kWarps;
+            const int j = tile * 8 + 2 * t4;
+            if (tile >= ntiles) continue;
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              const int m = g8 + 8 * hh;
+              if (m >= h.n) continue;
+              float* zr = zc + int64_t(h.tok[m]) * p.z_stride;
+              if (j < R) zr[j] = acc[i][2 * hh];
+              if (j + 1 < R) zr[j + 1] = acc[i][2 * hh + 1];
+            }
+          }
+        }
+      } else {
+        // ntiles < 8 and kparts * ntiles <= 8, so kparts * (8 * ntiles) <= 64.
+        const int RP = 8 * ntiles;
+        if (active) {
+          const int j = my_tile0 * 8 + 2 * t4;
+          float* wp = warp_part + my_kpart * kSeg * RP;
+          wp[g8 * RP + j] = acc[0][0];
+          wp[g8 * RP + j + 1] = acc[0][1];
+          wp[(g8 + 8) * RP + j] = acc[0][2];
+          wp[(g8 + 8) * RP + j + 1] = acc[0][3];
+        }
+        __syncthreads();
+        for (int i = tid; i < h.n * R; i += kThreads) {
+          const int m = i / R, j = i - m * R;
+          float sum = 0.f;
+          for (int q = 0; q < kparts; ++q) sum += warp_part[(q * kSeg + m) * RP + j];
+          zc[int64_t(h.tok[m]) * p.z_stride + j] = sum;
         }
       }
     }
+    __syncthreads();  // stage st and the partial buffer are free again
   }
-  __syncthreads();  // tiles are dead from here on: reuse them for the partial sums
-  float* warp_part = reinterpret_cast<float*>(tiles);         // [kparts][16][8*ntiles]
-  float* cta_part = reinterpret_cast<float*>(tiles) + kSeg * 64;  // [16][kMaxRows]
-  if (kparts == 1) {
-    // Warps beyond ntiles*kparts hold no tile (their accumulators are zero).
-#pragma unroll
-    for (int i = 0; i < kMaxTilesPerWarp; ++i) {
-      const int tile = my_tile0 + i * kWarps;
-      const int j = tile * 8 + 2 * t4;
-      if (active && tile < ntiles && j < R) {
-        cta_part[g8 * kMaxRows + j] = acc[i][0];
-        cta_part[(g8 + 8) * kMaxRows + j] = acc[i][2];
-      }
-      if (active && tile < ntiles && j + 1 < R) {
-        cta_part[g8 * kMaxRows + j + 1] = acc[i][1];
-        cta_part[(g8 + 8) * kMaxRows + j + 1] = acc[i][3];
-      }
-    }
-  } else {
-    // ntiles < 8 and kparts * ntiles <= 8, so kparts * (8 * ntiles) <= 64.
-    const int RP = 8 * ntiles;
-    if (active) {
-      const int j = my_tile0 * 8 + 2 * t4;
-      float* wp = warp_part + my_kpart * kSeg * RP;
-      wp[g8 * RP + j] = acc[0][0];
-      wp[g8 * RP + j + 1] = acc[0][1];
-      wp[(g8 + 8) * RP + j] = acc[0][2];
-      wp[(g8 + 8) * RP + j + 1] = acc[0][3];
-    }
-    __syncthreads();
-    for (int i = tid; i < kSeg * R; i += kThreads) {
-      const int m = i / R, j = i - m * R;
-      float sum = 0.f;
-      for (int q = 0; q < kparts; ++q) sum += warp_part[(q * kSeg + m) * RP + j];
-      cta_part[m * kMaxRows + j] = sum;
-    }
-  }
-  if (parts == 1) {
-    __syncthreads();
-    for (int i = tid; i < si.n * R; i += kThreads) {
-      const int m = i / R, j = i - m * R;
-      p.z[int64_t(tok[m]) * p.z_stride + j] = cta_part[m * kMaxRows + j];
-    }
-  } else {
-    // Rank 0 adds the cluster's partials in rank order and writes z.
-    cg::cluster_group cluster = cg::this_cluster();
-    cluster.sync();
-    if (rank == 0) {
-      for (int i = tid; i < si.n * R; i += kThreads) {
-        const int m = i / R, j = i - m * R;
-        float sum = 0.f;
-        for (int c = 0; c < parts; ++c) sum += cluster.map_shared_rank(cta_part, c)[m * kMaxRows + j];
-        p.z[int64_t(tok[m]) * p.z_stride + j] = sum;
-      }
-    }
-    cluster.sync();  // keep every CTA's partial alive until rank 0 has read it
-  }
+  cp_async_wait<0>();
   __syncthreads();
   pdl_launch_dependents();
+}
+
+// Shrink tiling for the host: K chunk width (a multiple of 64) and stage bytes such
+// that three stages of (16 + S*r) rows fit two CTAs per SM.
+struct ShrinkTiling {
+  int kc, stage_bytes, smem, nchunks;
+};
+
+inline ShrinkTiling shrink_tiling(int64_t width, int num_slices, int capacity) {
+  const int rows = kSeg + (num_slices * (capacity < 64 ? capacity : 64) + 7) / 8 * 8;
+  int kc = int((36 * 1024 / rows - 64) / 2) / 64 * 64;
+  if (kc > 512) kc = 512;
+  if (kc < 64) kc = 64;
+  const int64_t wpad = (width + 63) / 64 * 64;
+  if (kc > wpad) kc = int(wpad);
+  ShrinkTiling t;
+  t.kc = kc;
+  t.stage_bytes = (rows * (kc * 2 + 64) + 127) / 128 * 128;
+  t.smem = kShrinkStages * t.stage_bytes + kShrinkStages * int(sizeof(ShrinkHeader)) + kSeg * 64 * 4;
+  t.nchunks = int((width + kc - 1) / kc);
+  return t;
 }
 
 // ------------------------------------------------------------------ expand kernel
@@ -529,7 +597,7 @@ __global__ void __launch_bounds__(kThreads, 2) sgmv_expand_kernel(const __grid_c
     const int rem = i - m * p.S * si.kp;
     const int s = rem / si.kp, k = rem - s * si.kp;
     float v = 0.f;
-    if (k < live && m < si.n) v = p.z[int64_t(tok[m]) * p.z_stride + s * si.r + k];
+    if (k < live && m < si.n) v = z_value(p, tok[m], s * si.r + k);
     zs[(m * kMaxSlices + s) * kMaxKp + k] = v;
   }
   __syncthreads();
@@ -724,22 +792,17 @@ __device__ __forceinline__ void consume_item(const ItemHeader& h, const Stage& s
       if (m >= h.n) continue;
       uint2* yp = reinterpret_cast<uint2*>(yt + m * kYPitch + rc * 2);
       const uint2 old = *yp;
-      const uint32_t w[2] = {old.x, old.y};
-      uint32_t res[2];
+      const float b0 = __uint_as_float(old.x << 16), b1 = __uint_as_float(old.x & 0xffff0000u);
+      const float b2 = __uint_as_float(old.y << 16), b3 = __uint_as_float(old.y & 0xffff0000u);
+      float d[4];
 #pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        uint32_t bits2[2];
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const float base = bf16_bits_to_float((w[q] >> (16 * e)) & 0xffffu);
-          const float acc = out[hh][2 * q + e];
-          const float sum = MODE == kFp32
-                                ? base + h.scale * acc
-                                : base + bf16_bits_to_float(float_to_bf16_bits(acc * h.scale));
-          bits2[e] = float_to_bf16_bits(sum);
-        }
-        res[q] = pack2(bits2[0], bits2[1]);
+      for (int e = 0; e < 4; ++e) {
+        d[e] = MODE == kFp32 ? h.scale * out[hh][e]
+                             : bf16_bits_to_float(float_to_bf16_bits(out[hh][e] * h.scale));
       }
+      uint32_t res[2];
+      res[0] = cvt_bf16x2(b0 + d[0], b1 + d[1]);
+      res[1] = cvt_bf16x2(b2 + d[2], b3 + d[3]);
       *yp = make_uint2(res[0], res[1]);
     }
   }
@@ -851,7 +914,7 @@ sgmv_expand_bulk_kernel(const __grid_constant__ FusedParams p) {
             const int rem = i - m * p.S * kp;
             const int s = rem / kp, kk = rem - s * kp;
             zbuf[m * kMaxRows + s * kp + kk] =
-                (m < h.n && kk < live) ? p.z[int64_t(h.tok[m]) * p.z_stride + s * h.r + kk] : 0.f;
+                (m < h.n && kk < live) ? z_value(p, h.tok[m], s * h.r + kk) : 0.f;
           }
           named_barrier(1, kConsumers * 32);
         }
@@ -892,12 +955,20 @@ sgmv_expand_bulk_kernel(const __grid_constant__ FusedParams p) {
 
 using namespace lfb;
 
+extern "C" int64_t lf_fused_workspace_floats(int64_t num_tokens, int64_t width,
+                                             int32_t num_slices, int32_t capacity) {
+  if (num_tokens < 0 || width < 1 || num_slices < 1 || capacity < 1) return -1;
+  const ShrinkTiling t = shrink_tiling(width, num_slices, capacity);
+  const int64_t zstride = (int64_t(num_slices) * capacity + 3) / 4 * 4;
+  return int64_t(t.nchunks) * (num_tokens > 0 ? num_tokens : 1) * zstride;
+}
+
 extern "C" int lf_fused_shrink_expand(
     const void* x, int64_t x_stride, const void* a, const void* b, const int64_t* b_offsets,
     const int32_t* b_strides, void* y, int64_t y_stride, const int32_t* segment_indptr,
     const int32_t* segment_slots, const int32_t* token_indices, const int32_t* ranks,
     const float* scales, const int32_t* slice_offsets, const int32_t* segment_count,
-    float* workspace, int64_t workspace_stride, int64_t num_tokens, int64_t width,
+    float* workspace, int64_t workspace_floats, int64_t num_tokens, int64_t width,
     int32_t out_width, int32_t num_slices, int32_t capacity, int32_t num_slots,
     int32_t max_segments, int32_t numerics, void* stream) {
   if (num_tokens < 0 || num_tokens >= (int64_t(1) << 31) || width < 1 || width >= (int64_t(1) << 31))
@@ -908,143 +979,69 @@ extern "C" int lf_fused_shrink_expand(
     return fail(LF_E_INVALID, "fused_shrink_expand: x/A must be 16-byte aligned with width and stride multiples of 8");
   if (!aligned16(b) || (reinterpret_cast<uintptr_t>(y) & 7) || y_stride % 4 || y_stride < out_width)
     return fail(LF_E_INVALID, "fused_shrink_expand: B must be 16-byte aligned, y 8-byte aligned with stride a multiple of 4");
-  if (!workspace || workspace_stride < int64_t(num_slices) * capacity)
-    return fail(LF_E_INVALID, "fused_shrink_expand: workspace rows must hold num_slices*capacity floats");
   if (numerics != kFp32 && numerics != kReference)
     return fail(LF_E_INVALID, "fused_shrink_expand: numerics must be 0 (fp32) or 1 (reference)");
   if (max_segments < 0) return fail(LF_E_INVALID, "fused_shrink_expand: negative segment capacity");
+  const int64_t need = lf_fused_workspace_floats(num_tokens, width, num_slices, capacity);
+  if (!workspace || workspace_floats < need || (reinterpret_cast<uintptr_t>(workspace) & 15))
+    return fail(LF_E_INVALID, "fused_shrink_expand: workspace too small or not 16-byte aligned "
+                              "(see lf_fused_workspace_floats)");
   if (num_tokens == 0 || max_segments == 0) return LF_OK;
+  const ShrinkTiling tiling = shrink_tiling(width, num_slices, capacity);
   const int units = (out_width + 15) / 16;
-  const int units_per_chunk = 64;  // 1024 output columns per expand CTA
+  const int units_per_chunk = 64;  // direct expand: 1024 output columns per CTA
   const int chunks = (units + units_per_chunk - 1) / units_per_chunk;
   if (chunks > 65535 && max_segments > 65535)
     return fail(LF_E_INVALID, "fused_shrink_expand: grid too large");
+  const int64_t zstride = (int64_t(num_slices) * capacity + 3) / 4 * 4;
   FusedParams p{static_cast<const uint16_t*>(x), x_stride, static_cast<const uint16_t*>(a),
                 static_cast<const uint16_t*>(b), b_offsets, b_strides, static_cast<uint16_t*>(y),
                 y_stride, segment_indptr, segment_slots, token_indices, ranks, scales,
-                slice_offsets, segment_count, workspace, workspace_stride, int(num_tokens),
-                int(width), out_width, num_slices, capacity, num_slots, max_segments,
-                units_per_chunk};
-  // K is split over a cluster of `parts` CTAs (a power of two up to 16, non-portable
-  // above 8); each stages 16 token rows + S*r A rows (rounded up to the 8-row MMA
-  // tiles the fragment loads read) of its K slice.  Pick the smallest cluster whose
-  // slice fits ~72 KB, i.e. three CTAs per SM.
-  const int rows_max = kSeg + (num_slices * (capacity < 64 ? capacity : 64) + 7) / 8 * 8;
-  int parts = 1, kslice = int((width + 31) / 32 * 32);
-  while (parts < kMaxCluster && int64_t(rows_max) * (kslice * 2 + 64) > 72 * 1024) {
-    parts *= 2;
-    kslice = int(((width + parts - 1) / parts + 31) / 32 * 32);
-  }
-  const int tile_bytes = rows_max * (kslice * 2 + 64);
-  int smem = tile_bytes > (kSeg * 64 + kSeg * kMaxRows) * 4 ? tile_bytes
-                                                             : (kSeg * 64 + kSeg * kMaxRows) * 4;
-  if (smem > 220 * 1024) return fail(LF_E_INVALID, "fused_shrink_expand: K slice too large");
+                slice_offsets, segment_count, workspace, zstride, zstride * num_tokens,
+                int(num_tokens), int(width), out_width, num_slices, capacity, num_slots,
+                max_segments, tiling.nchunks, units_per_chunk};
+  int device = 0, sms = 0;
+  if (cudaGetDevice(&device) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
+    return check_launch("fused_shrink_expand: device query");
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   {
     static int flags[64] = {};
-    if (int rc = ensure_smem(sgmv_shrink_kernel, smem, flags)) return rc;
-    if (parts > 8) {
-      static unsigned long long np_flags = 0;
-      int device = 0;
-      cudaGetDevice(&device);
-      if (!(np_flags & (1ull << (device & 63)))) {
-        if (cudaFuncSetAttribute(sgmv_shrink_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed,
-                                 1) != cudaSuccess)
-          return check_launch("fused_shrink_expand: non-portable cluster size");
-        np_flags |= 1ull << (device & 63);
-      }
-    }
-    // Shrink the cluster (and grow the slice) until the hardware can co-schedule it.
-    while (parts > 1) {
-      cudaLaunchConfig_t probe = {};
-      probe.gridDim = dim3(parts, 1, 1);
-      probe.blockDim = dim3(kThreads);
-      probe.dynamicSmemBytes = smem;
-      cudaLaunchAttribute cattr[1];
-      cattr[0].id = cudaLaunchAttributeClusterDimension;
-      cattr[0].val.clusterDim.x = parts;
-      cattr[0].val.clusterDim.y = 1;
-      cattr[0].val.clusterDim.z = 1;
-      probe.attrs = cattr;
-      probe.numAttrs = 1;
-      int active = 0;
-      if (cudaOccupancyMaxActiveClusters(&active, sgmv_shrink_kernel, &probe) == cudaSuccess &&
-          active > 0)
-        break;
-      cudaGetLastError();
-      parts /= 2;
-      kslice = int(((width + parts - 1) / parts + 31) / 32 * 32);
-      const int bytes = rows_max * (kslice * 2 + 64);
-      if (bytes > smem) {
-        smem = bytes;
-        if (smem > 220 * 1024) return fail(LF_E_INVALID, "fused_shrink_expand: K slice too large");
-        if (int rc = ensure_smem(sgmv_shrink_kernel, smem, flags)) return rc;
-      }
-    }
-    cudaLaunchConfig_t config = {};
-    config.gridDim = dim3(parts, max_segments, 1);
-    config.blockDim = dim3(kThreads);
-    config.dynamicSmemBytes = smem;
-    config.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = parts;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    config.attrs = attr;
-    config.numAttrs = 1;
-    const cudaError_t err = cudaLaunchKernelEx(&config, sgmv_shrink_kernel, p, kslice);
-    if (err != cudaSuccess) {
-      last_error() = std::string("fused_shrink_expand (shrink): ") + cudaGetErrorString(err);
-      return LF_E_CUDA;
-    }
+    if (int rc = ensure_smem(sgmv_shrink_kernel, tiling.smem, flags)) return rc;
+    sgmv_shrink_kernel<<<2 * sms, kThreads, tiling.smem, s>>>(p, tiling.kc, tiling.stage_bytes);
+    if (int rc = check_launch("fused_shrink_expand (shrink)")) return rc;
   }
   // The bulk-copy expand needs 16-byte aligned y rows and 8-column multiples; other
   // layouts use the direct-load expand.
   const bool bulk = out_width % 8 == 0 && y_stride % 8 == 0 &&
                     (reinterpret_cast<uintptr_t>(y) & 15) == 0;
+  cudaLaunchConfig_t config = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  config.attrs = attr;
+  config.numAttrs = 1;
+  config.stream = s;
+  cudaError_t err;
   if (bulk) {
-    int device = 0, sms = 0;
-    if (cudaGetDevice(&device) != cudaSuccess ||
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
-      return check_launch("fused_shrink_expand: device query");
     auto kernel = numerics == kFp32 ? sgmv_expand_bulk_kernel<kFp32>
                                     : sgmv_expand_bulk_kernel<kReference>;
     static int flags[2][64] = {};
     if (int rc = ensure_smem(kernel, kTmaSmem, flags[numerics])) return rc;
-    cudaLaunchConfig_t config = {};
     config.gridDim = dim3(sms);
     config.blockDim = dim3(kTmaThreads);
     config.dynamicSmemBytes = kTmaSmem;
-    config.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    config.attrs = attr;
-    config.numAttrs = 1;
-    const cudaError_t err = cudaLaunchKernelEx(&config, kernel, p);
-    if (err != cudaSuccess) {
-      last_error() = std::string("fused_shrink_expand (expand): ") + cudaGetErrorString(err);
-      return LF_E_CUDA;
-    }
-    return LF_OK;
-  }
-  {
-    cudaLaunchConfig_t config = {};
+    err = cudaLaunchKernelEx(&config, kernel, p);
+  } else {
+    auto kernel = numerics == kFp32 ? sgmv_expand_kernel<kFp32> : sgmv_expand_kernel<kReference>;
     config.gridDim = dim3(chunks, max_segments, 1);
     config.blockDim = dim3(kThreads);
-    config.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    config.attrs = attr;
-    config.numAttrs = 1;
-    auto kernel = numerics == kFp32 ? sgmv_expand_kernel<kFp32> : sgmv_expand_kernel<kReference>;
-    const cudaError_t err = cudaLaunchKernelEx(&config, kernel, p);
-    if (err != cudaSuccess) {
-      last_error() = std::string("fused_shrink_expand (expand): ") + cudaGetErrorString(err);
-      return LF_E_CUDA;
-    }
+    config.dynamicSmemBytes = 0;
+    err = cudaLaunchKernelEx(&config, kernel, p);
+  }
+  if (err != cudaSuccess) {
+    last_error() = std::string("fused_shrink_expand (expand): ") + cudaGetErrorString(err);
+    return LF_E_CUDA;
   }
   return LF_OK;
 }

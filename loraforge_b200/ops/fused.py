@@ -24,6 +24,11 @@ from loraforge_b200.ops.lora_rows import _distinct_output, _tensor, _vector
 NUMERICS = {"fp32": 0, "reference": 1}
 
 
+def workspace_floats(tokens: int, width: int, num_slices: int, capacity: int) -> int:
+    """Elements of the FP32 workspace ``lora_shrink_expand`` needs for these sizes."""
+    return _native.fused_workspace_floats(tokens, width, num_slices, capacity)
+
+
 @ExperimentalAPI(reason="Fused BF16 decode shrink/expand; sm_100a tensor cores, caller-owned metadata.")
 def lora_shrink_expand(
     x,
@@ -50,8 +55,9 @@ def lora_shrink_expand(
     slice_offsets partitioning N; B flat with b_offsets (8-element aligned) and
     power-of-two b_strides in 1..64; segments of at most 16 tokens, one slot each
     (``group_tokens(..., chunk=16)``).  Slot -1 / rank-0 segments leave output
-    unchanged.  ``workspace`` is an optional FP32 [tokens, slices*capacity] buffer
-    for the intermediate (allocated per call when omitted; pass one to keep a
+    unchanged.  ``workspace`` is an optional FP32 buffer of at least
+    ``workspace_floats(tokens, width, num_slices, capacity)`` elements for the
+    shrink's partial sums (allocated per call when omitted; pass one to keep a
     captured graph allocation-free).
     """
     import torch
@@ -104,18 +110,21 @@ def lora_shrink_expand(
          token_indices, slice_offsets, segment_count),
     )
     capacity = a.shape[1] // num_slices
+    need = _native.fused_workspace_floats(x.shape[0], x.shape[1], num_slices, capacity)
     if workspace is None:
-        workspace = torch.empty(x.shape[0], num_slices * capacity, dtype=torch.float32, device=x.device)
+        workspace = torch.empty(need, dtype=torch.float32, device=x.device)
     if (
         not isinstance(workspace, torch.Tensor)
         or workspace.dtype != torch.float32
         or workspace.device != x.device
-        or workspace.ndim != 2
-        or workspace.shape[0] < x.shape[0]
-        or workspace.shape[1] < num_slices * capacity
-        or workspace.stride(1) != 1
+        or not workspace.is_contiguous()
+        or workspace.numel() < need
+        or workspace.data_ptr() % 16
     ):
-        raise ValueError("workspace must be FP32 [tokens, slices*capacity] on the same device")
+        raise ValueError(
+            f"workspace must be a contiguous 16-byte aligned FP32 buffer of >= {need} "
+            "elements on the same device (workspace_floats)"
+        )
     if x.shape[0] == 0:
         return
     with torch.cuda.device(x.device):
@@ -137,7 +146,7 @@ def lora_shrink_expand(
             slice_offsets.data_ptr(),
             segment_count.data_ptr(),
             workspace.data_ptr(),
-            workspace.stride(0),
+            workspace.numel(),
             x.shape[0],
             x.shape[1],
             output.shape[1],

@@ -14,7 +14,7 @@ HEADER = ROOT / "include" / "loraforge_b200.h"
 
 def declared_symbols():
     text = HEADER.read_text()
-    return sorted(set(re.findall(r"^(?:int|const char\*)\s+(lf_\w+)\(", text, re.M)))
+    return sorted(set(re.findall(r"^(?:int64_t|int|const char\*)\s+(lf_\w+)\(", text, re.M)))
 
 
 def test_header_and_binding_agree():
