@@ -67,15 +67,23 @@ struct FusedParams {
   int64_t z_stride;        // >= S * cap, a multiple of 4
   int64_t z_chunk;         // floats per chunk partial (T * z_stride)
   int T, K, N, S, cap, num_slots, max_segments;
-  int nchunks;             // K chunks of the shrink (partials to add per z value)
+  int nchunks;             // K chunks of the shrink (slots of partials per token)
+  int shrink_ctas;         // grid size of the shrink (defines its per-CTA unit runs)
   int units_per_chunk;     // direct expand: 16-column units per CTA
 };
 
-// Sum of the shrink's chunk partials for token `tok`, packed column `j`.
-__device__ __forceinline__ float z_value(const FusedParams& p, int tok, int j) {
+// z[tok, j] for a token of segment `seg`: the sum, in chunk order, of the partials
+// the shrink wrote.  The shrink gives each CTA a contiguous run of (segment, chunk)
+// units and writes one partial per (segment, CTA run), at the slot of the run's first
+// chunk; the run starts are the segment's first chunk and every CTA boundary inside
+// the segment.
+__device__ __forceinline__ float z_value(const FusedParams& p, int nseg, int seg, int tok, int j) {
+  const int64_t nunits = int64_t(nseg) * p.nchunks;
+  const int64_t per = (nunits + p.shrink_ctas - 1) / p.shrink_ctas;
+  const int64_t first = int64_t(seg) * p.nchunks, last = first + p.nchunks;
   const float* zp = p.z + int64_t(tok) * p.z_stride + j;
-  float sum = 0.f;
-  for (int c = 0; c < p.nchunks; ++c) sum += zp[c * p.z_chunk];
+  float sum = zp[0];
+  for (int64_t b = (first / per + 1) * per; b < last; b += per) sum += zp[(b - first) * p.z_chunk];
   return sum;
 }
 
@@ -467,50 +475,55 @@ sgmv_shrink_kernel(const __grid_constant__ FusedParams p, int kc, int stage_byte
 
   issue(u0, 0);
   issue(u0 + 1, 1);
+  // Accumulators persist over consecutive units of one segment (a "run"); a run's
+  // partial is written at the slot of its first chunk when the run ends.
+  float acc[kMaxTilesPerWarp][4];
+#pragma unroll
+  for (int i = 0; i < kMaxTilesPerWarp; ++i)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[i][e] = 0.f;
   for (int u = u0, k = 0; u < u1; ++u, ++k) {
     const int st = k % kShrinkStages;
     issue(u + 2, (k + 2) % kShrinkStages);
     cp_async_wait<2>();  // unit u's group has landed
     __syncthreads();
     const ShrinkHeader& h = hdr[st];
-    if (h.ok) {
+    const int seg = u / p.nchunks;
+    const bool run_end = u + 1 == u1 || (u + 1) / p.nchunks != seg;
+    const int R = p.S * h.r;
+    const int ntiles = (R + 7) / 8;
+    const int kparts = ntiles >= kWarps ? 1 : kWarps / ntiles;
+    const int my_tile0 = ntiles >= kWarps ? warp : warp % ntiles;
+    const int my_kpart = ntiles >= kWarps ? 0 : warp / ntiles;
+    const bool active = my_kpart < kparts;
+    if (h.ok && active) {
       const uint8_t* base = smem + st * stage_bytes;
       const int klen = min(p.K, (h.chunk + 1) * kc) - h.chunk * kc;
-      const int R = p.S * h.r;
-      const int ntiles = (R + 7) / 8;
-      const int kparts = ntiles >= kWarps ? 1 : kWarps / ntiles;
-      const int my_tile0 = ntiles >= kWarps ? warp : warp % ntiles;
-      const int my_kpart = ntiles >= kWarps ? 0 : warp / ntiles;
-      const bool active = my_kpart < kparts;
-      float acc[kMaxTilesPerWarp][4];
-#pragma unroll
-      for (int i = 0; i < kMaxTilesPerWarp; ++i)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[i][e] = 0.f;
-      if (active) {
-        const int kblocks = (klen + 31) / 32;
-        const int b0 = kblocks * my_kpart / kparts, b1 = kblocks * (my_kpart + 1) / kparts;
-        const uint8_t* xr0 = base + g8 * pitch;
-        const uint8_t* xr1 = base + (g8 + 8) * pitch;
-        const uint4 zero = make_uint4(0, 0, 0, 0);
+      const int kblocks = (klen + 31) / 32;
+      const int b0 = kblocks * my_kpart / kparts, b1 = kblocks * (my_kpart + 1) / kparts;
+      const uint8_t* xr0 = base + g8 * pitch;
+      const uint8_t* xr1 = base + (g8 + 8) * pitch;
+      const uint4 zero = make_uint4(0, 0, 0, 0);
 #pragma unroll 4
-        for (int blk = b0; blk < b1; ++blk) {
-          const int kk = blk * 32 + 8 * t4;
-          const bool kin = kk < klen;
-          const uint4 x0 = kin ? lds16(xr0 + kk * 2) : zero;
-          const uint4 x1 = kin ? lds16(xr1 + kk * 2) : zero;
+      for (int blk = b0; blk < b1; ++blk) {
+        const int kk = blk * 32 + 8 * t4;
+        const bool kin = kk < klen;
+        const uint4 x0 = kin ? lds16(xr0 + kk * 2) : zero;
+        const uint4 x1 = kin ? lds16(xr1 + kk * 2) : zero;
 #pragma unroll
-          for (int i = 0; i < kMaxTilesPerWarp; ++i) {
-            const int tile = my_tile0 + i * kWarps;
-            if (tile < ntiles) {
-              const uint4 av = kin ? lds16(base + (kSeg + tile * 8 + g8) * pitch + kk * 2) : zero;
-              mma16816(acc[i], x0.x, x1.x, x0.y, x1.y, av.x, av.y);
-              mma16816(acc[i], x0.z, x1.z, x0.w, x1.w, av.z, av.w);
-            }
+        for (int i = 0; i < kMaxTilesPerWarp; ++i) {
+          const int tile = my_tile0 + i * kWarps;
+          if (tile < ntiles) {
+            const uint4 av = kin ? lds16(base + (kSeg + tile * 8 + g8) * pitch + kk * 2) : zero;
+            mma16816(acc[i], x0.x, x1.x, x0.y, x1.y, av.x, av.y);
+            mma16816(acc[i], x0.z, x1.z, x0.w, x1.w, av.z, av.w);
           }
         }
       }
-      float* zc = p.z + int64_t(h.chunk) * p.z_chunk;
+    }
+    if (run_end && h.ok) {
+      const int slot = max(u0, seg * p.nchunks) - seg * p.nchunks;
+      float* zc = p.z + int64_t(slot) * p.z_chunk;
       if (kparts == 1) {
         // Warps beyond ntiles hold no tile.  Rows m >= n belong to no token.
         if (active) {
@@ -548,6 +561,12 @@ sgmv_shrink_kernel(const __grid_constant__ FusedParams p, int kc, int stage_byte
           zc[int64_t(h.tok[m]) * p.z_stride + j] = sum;
         }
       }
+    }
+    if (run_end) {
+#pragma unroll
+      for (int i = 0; i < kMaxTilesPerWarp; ++i)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[i][e] = 0.f;
     }
     __syncthreads();  // stage st and the partial buffer are free again
   }
@@ -589,6 +608,7 @@ __global__ void __launch_bounds__(kThreads, 2) sgmv_expand_kernel(const __grid_c
   SegmentInfo si;
   int start = 0;
   if (!load_segment(p, blockIdx.y, si, start)) return;
+  const int nseg = min(*p.seg_count, p.max_segments);
   if (tid <= p.S) offs[tid] = p.slice_offsets[tid];
   if (!load_tokens(p, si, start, tok)) return;
   const int live = min(si.r, si.bucket);
@@ -597,7 +617,7 @@ __global__ void __launch_bounds__(kThreads, 2) sgmv_expand_kernel(const __grid_c
     const int rem = i - m * p.S * si.kp;
     const int s = rem / si.kp, k = rem - s * si.kp;
     float v = 0.f;
-    if (k < live && m < si.n) v = z_value(p, tok[m], s * si.r + k);
+    if (k < live && m < si.n) v = z_value(p, nseg, blockIdx.y, tok[m], s * si.r + k);
     zs[(m * kMaxSlices + s) * kMaxKp + k] = v;
   }
   __syncthreads();
@@ -620,10 +640,9 @@ __global__ void __launch_bounds__(kThreads, 2) sgmv_expand_kernel(const __grid_c
 // (at most 32 KB of B rows) and streams the stage's B rows and y rows into a
 // kStages-deep shared-memory ring with cp.async.bulk, completion tracked by the
 // stage's "full" mbarrier.  Warps 0..kConsumers-1 compute a stage on the tensor cores
-// from shared memory and write y back into it; consumer thread 0 bulk-stores the y
-// rows and releases the previous stage (whose stores have been read by then) through
-// its "empty" mbarrier, so the stores of one stage overlap the next stage's compute.
-// A header with ok = -1 ends the stream.
+// from shared memory, store the updated y values straight to global memory (8 bytes
+// per lane, so the stage is free as soon as the compute is done) and release the
+// stage through its "empty" mbarrier.  A header with ok = -1 ends the stream.
 constexpr int kStages = 3;
 constexpr int kItemCols = 256;
 constexpr int kStageCols = 1024;
@@ -656,8 +675,8 @@ struct Stage {
 // zbuf: the segment's z, FP32 [kSeg][kMaxRows], zero beyond each slice's live rank.
 template <int KP, int MODE>
 __device__ __forceinline__ void consume_item(const ItemHeader& h, const Stage& st, int S, int N,
-                                             const int* offs, const float* zbuf, int lane,
-                                             int warp) {
+                                             const int* offs, const float* zbuf, uint16_t* y,
+                                             int64_t y_stride, int lane, int warp) {
   constexpr int KSTEPS = KP >= 16 ? KP / 16 : 1;
   const int g = lane >> 2, t = lane & 3;
   const uint16_t* bt = st.btile();
@@ -740,6 +759,9 @@ __device__ __forceinline__ void consume_item(const ItemHeader& h, const Stage& s
   };
 
   const int units = (h.ncols + 15) / 16;
+  // Usually the whole stage lies in one slice; then no per-unit slice lookups.
+  const int stage_first = slice_of(h.col0);
+  const int stage_slice = stage_first == slice_of(h.col0 + h.ncols - 1) ? stage_first : -1;
   for (int u = warp; u < units; u += kConsumers) {
     const int r0 = u * 16;  // first column of the unit, relative to col0
     const int n0 = h.col0 + r0;
@@ -747,32 +769,44 @@ __device__ __forceinline__ void consume_item(const ItemHeader& h, const Stage& s
     uint32_t bfr[2][KSTEPS][2];
     load_b(rb, rb < h.ncols, bfr[0]);
     load_b(rb + 2, rb + 2 < h.ncols, bfr[1]);
-    const int s_first = slice_of(n0);
-    const int s_last = slice_of(min(n0 + 15, N - 1));
+    const int s_first = stage_slice >= 0 ? stage_slice : slice_of(n0);
+    const int s_last = stage_slice >= 0 ? stage_slice : slice_of(min(n0 + 15, N - 1));
     float out[2][4];
     for (int s = s_first; s <= s_last; ++s) {
       if (s != cached_slice) {
         load_z(s);
         cached_slice = s;
       }
-      float acc[2][4];
+      // Separate accumulators per tile and per hi/lo part: four independent MMA chains.
+      constexpr int PARTS = MODE == kFp32 ? 2 : 1;
+      float accp[2][PARTS][4];
 #pragma unroll
-      for (int tile = 0; tile < 2; ++tile) {
+      for (int tile = 0; tile < 2; ++tile)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) acc[tile][i] = 0.f;
+        for (int part = 0; part < PARTS; ++part)
 #pragma unroll
-        for (int ks = 0; ks < KSTEPS; ++ks) {
+          for (int i = 0; i < 4; ++i) accp[tile][part][i] = 0.f;
 #pragma unroll
-          for (int part = 0; part < (MODE == kFp32 ? 2 : 1); ++part) {
+      for (int ks = 0; ks < KSTEPS; ++ks) {
+#pragma unroll
+        for (int tile = 0; tile < 2; ++tile) {
+#pragma unroll
+          for (int part = 0; part < PARTS; ++part) {
             if constexpr (KP == 8) {
-              mma1688(acc[tile], zf[ks][part][0], zf[ks][part][1], bfr[tile][ks][0]);
+              mma1688(accp[tile][part], zf[ks][part][0], zf[ks][part][1], bfr[tile][ks][0]);
             } else {
-              mma16816(acc[tile], zf[ks][part][0], zf[ks][part][1], zf[ks][part][2],
+              mma16816(accp[tile][part], zf[ks][part][0], zf[ks][part][1], zf[ks][part][2],
                        zf[ks][part][3], bfr[tile][ks][0], bfr[tile][ks][1]);
             }
           }
         }
       }
+      float acc[2][4];
+#pragma unroll
+      for (int tile = 0; tile < 2; ++tile)
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          acc[tile][i] = PARTS == 2 ? accp[tile][0][i] + accp[tile][PARTS - 1][i] : accp[tile][0][i];
       const float v[2][4] = {{acc[0][0], acc[0][1], acc[1][0], acc[1][1]},
                              {acc[0][2], acc[0][3], acc[1][2], acc[1][3]}};
 #pragma unroll
@@ -790,8 +824,8 @@ __device__ __forceinline__ void consume_item(const ItemHeader& h, const Stage& s
     for (int hh = 0; hh < 2; ++hh) {
       const int m = g + 8 * hh;
       if (m >= h.n) continue;
-      uint2* yp = reinterpret_cast<uint2*>(yt + m * kYPitch + rc * 2);
-      const uint2 old = *yp;
+      const uint2 old = *reinterpret_cast<const uint2*>(yt + m * kYPitch + rc * 2);
+      uint2* yp = reinterpret_cast<uint2*>(y + int64_t(h.tok[m]) * y_stride + h.col0 + rc);
       const float b0 = __uint_as_float(old.x << 16), b1 = __uint_as_float(old.x & 0xffff0000u);
       const float b2 = __uint_as_float(old.y << 16), b3 = __uint_as_float(old.y & 0xffff0000u);
       float d[4];
@@ -895,7 +929,8 @@ sgmv_expand_bulk_kernel(const __grid_constant__ FusedParams p) {
     }
   } else {
     // ---------------- consumer warps
-    int zseg = -1, prev_stage = -1;
+    const int nseg = min(*p.seg_count, p.max_segments);
+    int zseg = -1;
     for (int k = 0;; ++k) {
       const int stage = k % kStages;
       const uint32_t phase = uint32_t(k / kStages) & 1u;
@@ -914,38 +949,19 @@ sgmv_expand_bulk_kernel(const __grid_constant__ FusedParams p) {
             const int rem = i - m * p.S * kp;
             const int s = rem / kp, kk = rem - s * kp;
             zbuf[m * kMaxRows + s * kp + kk] =
-                (m < h.n && kk < live) ? z_value(p, h.tok[m], s * h.r + kk) : 0.f;
+                (m < h.n && kk < live) ? z_value(p, nseg, h.seg, h.tok[m], s * h.r + kk) : 0.f;
           }
           named_barrier(1, kConsumers * 32);
         }
         switch (kp) {
-          case 8: consume_item<8, MODE>(h, st, p.S, p.N, offs, zbuf, lane, warp); break;
-          case 16: consume_item<16, MODE>(h, st, p.S, p.N, offs, zbuf, lane, warp); break;
-          case 32: consume_item<32, MODE>(h, st, p.S, p.N, offs, zbuf, lane, warp); break;
-          default: consume_item<64, MODE>(h, st, p.S, p.N, offs, zbuf, lane, warp); break;
-        }
-        fence_async_smem();
-      }
-      named_barrier(1, kConsumers * 32);
-      if (tid == 0) {
-        if (h.ok) {
-          for (int m = 0; m < h.n; ++m)
-            bulk_s2g(p.y + int64_t(h.tok[m]) * p.y_stride + h.col0, st.ytile() + m * kYPitch,
-                     uint32_t(h.ncols) * 2);
-        }
-        bulk_commit();
-        // The previous stage's stores have been read once at most this stage's group
-        // is pending; release it then.
-        if (prev_stage >= 0) {
-          asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-          mbar_arrive(&empty[prev_stage]);
+          case 8: consume_item<8, MODE>(h, st, p.S, p.N, offs, zbuf, p.y, p.y_stride, lane, warp); break;
+          case 16: consume_item<16, MODE>(h, st, p.S, p.N, offs, zbuf, p.y, p.y_stride, lane, warp); break;
+          case 32: consume_item<32, MODE>(h, st, p.S, p.N, offs, zbuf, p.y, p.y_stride, lane, warp); break;
+          default: consume_item<64, MODE>(h, st, p.S, p.N, offs, zbuf, p.y, p.y_stride, lane, warp); break;
         }
       }
-      prev_stage = stage;
-    }
-    if (tid == 0) {
-      bulk_wait_all();
-      if (prev_stage >= 0) mbar_arrive(&empty[prev_stage]);
+      named_barrier(1, kConsumers * 32);  // every warp is done with this stage
+      if (tid == 0) mbar_arrive(&empty[stage]);
     }
   }
 }
@@ -999,16 +1015,17 @@ extern "C" int lf_fused_shrink_expand(
                 y_stride, segment_indptr, segment_slots, token_indices, ranks, scales,
                 slice_offsets, segment_count, workspace, zstride, zstride * num_tokens,
                 int(num_tokens), int(width), out_width, num_slices, capacity, num_slots,
-                max_segments, tiling.nchunks, units_per_chunk};
+                max_segments, tiling.nchunks, 0, units_per_chunk};
   int device = 0, sms = 0;
   if (cudaGetDevice(&device) != cudaSuccess ||
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
     return check_launch("fused_shrink_expand: device query");
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  p.shrink_ctas = 2 * sms;
   {
     static int flags[64] = {};
     if (int rc = ensure_smem(sgmv_shrink_kernel, tiling.smem, flags)) return rc;
-    sgmv_shrink_kernel<<<2 * sms, kThreads, tiling.smem, s>>>(p, tiling.kc, tiling.stage_bytes);
+    sgmv_shrink_kernel<<<p.shrink_ctas, kThreads, tiling.smem, s>>>(p, tiling.kc, tiling.stage_bytes);
     if (int rc = check_launch("fused_shrink_expand (shrink)")) return rc;
   }
   // The bulk-copy expand needs 16-byte aligned y rows and 8-column multiples; other
