@@ -183,6 +183,34 @@ int64_t lf_fused_workspace_floats(int64_t num_tokens, int64_t width, int32_t num
                                   int32_t capacity);
 
 /*
+ * lf_fused_shrink_expand without a caller-provided workspace.  No counterpart in the
+ * reference.  Some callers cannot allocate device memory: serving engines that hand
+ * all free GPU memory to their own KV-cache pool at start-up and forbid later
+ * cudaMalloc calls, and foreign-language hosts (cgo, JNI, N-API) that have no access
+ * to the framework's caching allocator and must not create untracked allocations.
+ * This entry point allocates nothing (no cudaMalloc, cudaFree or allocating library
+ * call): its scratch is a 16 MiB array (4 Mi floats) compiled into the library, which
+ * every GPU that loads the library holds until the process exits.  Sizes whose
+ * lf_fused_workspace_floats(...) exceeds 4 Mi floats are rejected with LF_E_INVALID.
+ * The first call on a device looks up the buffer's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call before any
+ * stream capture.  All calls on a device share the buffer and it keeps the last call's
+ * contents (every value a call reads is written earlier in the same call, so nothing
+ * needs clearing); calls that overlap on the GPU (other streams, or graphs replayed
+ * concurrently) race on it and must be serialised by the caller.
+ */
+int lf_fused_shrink_expand_noalloc(const void* x, int64_t x_stride, const void* a,
+                                   const void* b, const int64_t* b_offsets,
+                                   const int32_t* b_strides, void* y, int64_t y_stride,
+                                   const int32_t* segment_indptr, const int32_t* segment_slots,
+                                   const int32_t* token_indices, const int32_t* ranks,
+                                   const float* scales, const int32_t* slice_offsets,
+                                   const int32_t* segment_count, int64_t num_tokens,
+                                   int64_t width, int32_t out_width, int32_t num_slices,
+                                   int32_t capacity, int32_t num_slots, int32_t max_segments,
+                                   int32_t numerics, void* stream);
+
+/*
  * Number of bounded device-side waits (mbarrier polls in the bulk-copy kernels)
  * that expired since the last reset; a non-zero count means a kernel gave up and
  * skipped work instead of hanging.  Synchronous; reset != 0 clears the counter.

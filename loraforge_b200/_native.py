@@ -52,6 +52,10 @@ SIGNATURES = {
         _p, _i64, _p, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _i64,
         _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _p,
     ],
+    "lf_fused_shrink_expand_noalloc": [
+        _p, _i64, _p, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _p,
+        _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _p,
+    ],
     "lf_device_wait_timeouts": [_p, _i32],
 }
 

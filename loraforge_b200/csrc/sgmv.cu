@@ -1075,3 +1075,63 @@ extern "C" int lf_device_wait_timeouts(int32_t* count, int32_t reset) {
   }
   return LF_OK;
 }
+
+// ------------------------------------------------------------------ allocation-free entry
+// lf_fused_shrink_expand_noalloc runs the same two kernels as lf_fused_shrink_expand
+// but takes its scratch from a fixed buffer compiled into this library, for callers
+// that are not allowed to allocate device memory themselves.
+#include <mutex>
+
+namespace {
+// 4 Mi floats (16 MiB).  A static __device__ array is created on every GPU that loads
+// this library and lives until the process exits.
+constexpr int64_t kNoAllocScratchFloats = int64_t(4) << 20;
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+
+std::mutex g_noalloc_mutex;
+float* g_noalloc_address[64] = {};  // device address of the buffer, per device
+}  // namespace
+
+extern "C" int lf_fused_shrink_expand_noalloc(
+    const void* x, int64_t x_stride, const void* a, const void* b, const int64_t* b_offsets,
+    const int32_t* b_strides, void* y, int64_t y_stride, const int32_t* segment_indptr,
+    const int32_t* segment_slots, const int32_t* token_indices, const int32_t* ranks,
+    const float* scales, const int32_t* slice_offsets, const int32_t* segment_count,
+    int64_t num_tokens, int64_t width, int32_t out_width, int32_t num_slices, int32_t capacity,
+    int32_t num_slots, int32_t max_segments, int32_t numerics, void* stream) {
+  const int64_t need = lf_fused_workspace_floats(num_tokens, width, num_slices, capacity);
+  if (need < 0) return fail(LF_E_INVALID, "fused_shrink_expand_noalloc: invalid sizes");
+  if (need > kNoAllocScratchFloats) {
+    last_error() = "fused_shrink_expand_noalloc: these sizes need " + std::to_string(need) +
+                   " floats of scratch, more than the built-in " +
+                   std::to_string(kNoAllocScratchFloats) +
+                   "-float (16 MiB) buffer; use lf_fused_shrink_expand with a workspace";
+    return LF_E_INVALID;
+  }
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return check_launch("fused_shrink_expand_noalloc");
+  if (device < 0 || device >= 64)
+    return fail(LF_E_UNSUPPORTED, "fused_shrink_expand_noalloc: device index above 63");
+  float* scratch = nullptr;
+  {
+    // First call on a device: look up the buffer's device address with that device
+    // current.  The host-side name g_noalloc_scratch is not a device address.
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (!g_noalloc_address[device]) {
+      void* address = nullptr;
+      const cudaError_t err = cudaGetSymbolAddress(&address, g_noalloc_scratch);
+      if (err != cudaSuccess || !address) {
+        last_error() = std::string("fused_shrink_expand_noalloc: cudaGetSymbolAddress: ") +
+                       cudaGetErrorString(err);
+        return LF_E_CUDA;
+      }
+      g_noalloc_address[device] = static_cast<float*>(address);
+    }
+    scratch = g_noalloc_address[device];
+  }
+  return lf_fused_shrink_expand(x, x_stride, a, b, b_offsets, b_strides, y, y_stride,
+                                segment_indptr, segment_slots, token_indices, ranks, scales,
+                                slice_offsets, segment_count, scratch, kNoAllocScratchFloats,
+                                num_tokens, width, out_width, num_slices, capacity, num_slots,
+                                max_segments, numerics, stream);
+}
