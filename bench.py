@@ -1,13 +1,17 @@
 """Multi-LoRA shrink+expand benchmark (BASELINE.json metric) on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config 1|2|3] [--path fused|rows]
 
-Workload: one decode batch of 256 tokens at Llama-3-8B
-projection shapes with 128 resident rank-16 adapters, adapter ids Zipf(1.1); the
-three projections fused QKV (4096 -> 4096/1024/1024), gate/up (4096 -> 2 x 14336)
-and down (14336 -> 4096).  x ~ N(0,1), A ~ N(0,1/K), B ~ N(0,1/r), scale 2.0, all
-BF16, seeded synthetic data.  One step = device grouping of the batch by adapter
-+ shrink + expand of the three projections.
+Default workload (the headline): one decode batch of 256
+tokens at Llama-3-8B projection shapes with 128 resident rank-16 adapters, adapter
+ids Zipf(1.1); the three projections fused QKV (4096 -> 4096/1024/1024), gate/up
+(4096 -> 2 x 14336) and down (14336 -> 4096).  x ~ N(0,1), A ~ N(0,1/K),
+B ~ N(0,1/r), scale 2.0, all BF16, seeded synthetic data.  Config 2 (512 tokens,
+256 retained-rank adapters, ranks U{4,8,16,32,64}, compact B, rsLoRA scales) and
+config 3 (8192-token prefill in 32 geometric segments, 64 rank-64 adapters, 5120)
+use the same harness.  One step = device grouping of the batch by adapter + shrink
++ expand of every projection.
 
 ``value``   tokens/s of the step replayed as a CUDA graph with inputs resident in
             HBM; L2 is flushed (a write larger than L2) before every timed step and
@@ -38,16 +42,7 @@ from pathlib import Path
 import numpy as np
 
 ROOT = Path(__file__).resolve().parent
-T_TOKENS = 256
-N_SLOTS = 128
-RANK = 16
-ZIPF_S = 1.1
-SCALE = 2.0
-PROJECTIONS = (  # name, in_dim, slice widths
-    ("qkv_proj", 4096, (4096, 1024, 1024)),
-    ("gate_up_proj", 4096, (14336, 14336)),
-    ("down_proj", 14336, (4096,)),
-)
+METRIC = "multi-LoRA shrink+expand tokens/s"
 
 
 def parse_args():
@@ -56,6 +51,7 @@ def parse_args():
     p.add_argument("--steps", type=int, default=300)
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--config", type=int, choices=sorted(CONFIGS), default=1)
     p.add_argument("--seed", type=int, default=1234)
     p.add_argument("--path", choices=("fused", "rows"), default="fused")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -64,94 +60,167 @@ def parse_args():
     return p.parse_args()
 
 
-# ----------------------------------------------------------------------------- workload
+# ----------------------------------------------------------------------------- workloads
 def zipf_slots(rng, tokens, slots, s):
     ranks = np.arange(1, slots + 1, dtype=np.float64)
     p = ranks**-s
     return rng.choice(slots, size=tokens, p=p / p.sum()).astype(np.int32)
 
 
+def geometric_segments(rng, tokens, segments, mean):
+    """Contiguous segment lengths: geometric (mean `mean`, min 1), rescaled to sum `tokens`."""
+    lengths = rng.geometric(1.0 / mean, size=segments).astype(np.float64)
+    lengths = np.maximum(1, np.floor(lengths * tokens / lengths.sum())).astype(np.int64)
+    lengths[np.argmax(lengths)] += tokens - lengths.sum()
+    return lengths
+
+
+def next_pow2(r):
+    return 1 << (max(1, int(r)) - 1).bit_length()
+
+
+# BASELINE.json configs (shapes and distributions); config 1 is the headline.
+CONFIGS = {
+    1: dict(
+        workload="config1: decode BGMV, Llama-3-8B qkv/gate_up/down, 256 tokens, 128 adapters "
+        "r=16, Zipf(1.1)",
+        tokens=256, slots=128, cap=16,
+        projections=(("qkv_proj", 4096, (4096, 1024, 1024)),
+                     ("gate_up_proj", 4096, (14336, 14336)),
+                     ("down_proj", 14336, (4096,))),
+    ),
+    2: dict(
+        workload="config2: retained-rank decode, 512 tokens, 256 adapters, ranks U{4..64}, "
+        "compact B, rsLoRA alpha=16, 4096->4096",
+        tokens=512, slots=256, cap=64, projections=(("proj", 4096, (4096,)),),
+    ),
+    3: dict(
+        workload="config3: prefill SGMV, 8192 tokens in 32 geometric segments (mean 256), "
+        "64 adapters r=64, 5120->5120",
+        tokens=8192, slots=64, cap=64, projections=(("proj", 5120, (5120,)),),
+    ),
+}
+
+
+def config_routing(config, rng):
+    """Per-slot ranks, scales and the token -> slot routing of a config."""
+    c = CONFIGS[config]
+    T, G = c["tokens"], c["slots"]
+    if config == 1:
+        ranks = np.full(G, 16)
+        scales = np.full(G, 2.0)
+        slots = zipf_slots(rng, T, G, 1.1)
+    elif config == 2:
+        ranks = rng.choice([4, 8, 16, 32, 64], size=G)
+        scales = 16.0 / np.sqrt(ranks)
+        slots = rng.integers(0, G, size=T).astype(np.int32)
+    else:
+        ranks = np.full(G, 64)
+        scales = np.full(G, 2.0)
+        lengths = geometric_segments(rng, T, 32, 256)
+        owners = rng.integers(0, G, size=len(lengths))
+        slots = np.repeat(owners, lengths).astype(np.int32)
+    return ranks.astype(np.int32), scales.astype(np.float32), slots
+
+
 class Projection:
-    def __init__(self, name, k, widths, device, gen):
+    """One LoRA-augmented projection: packed A, compact B store, per-slot metadata."""
+
+    def __init__(self, name, k, widths, ranks, scales, cap, tokens, device, gen):
         import torch
+
+        from loraforge_b200.ops.fused import workspace_floats
 
         self.name, self.K, self.widths = name, k, widths
         self.S, self.N = len(widths), sum(widths)
-        S, N, K = self.S, self.N, k
-        self.a = (torch.randn(N_SLOTS, S * RANK, K, generator=gen, device=device) / K**0.5).bfloat16()
-        self.b = (torch.randn(N_SLOTS * N * RANK, generator=gen, device=device) / RANK**0.5).bfloat16()
-        self.b_offsets = torch.arange(N_SLOTS, dtype=torch.int64, device=device) * (N * RANK)
-        self.b_strides = torch.full((N_SLOTS,), RANK, dtype=torch.int32, device=device)
-        self.ranks = torch.full((N_SLOTS,), RANK, dtype=torch.int32, device=device)
-        self.scales = torch.full((N_SLOTS,), SCALE, dtype=torch.float32, device=device)
+        self.cap, self.ranks_np, self.scales_np = cap, ranks, scales
+        G, S, N, K = len(ranks), self.S, self.N, k
+        self.a = (torch.randn(G, S * cap, K, generator=gen, device=device) / K**0.5).bfloat16()
+        buckets = np.array([next_pow2(r) for r in ranks])
+        offsets = np.concatenate(([0], np.cumsum(N * buckets)[:-1]))  # multiples of 8
+        self.b = torch.randn(int(N * buckets.sum()), generator=gen, device=device).bfloat16()
+        for g in range(G):  # B ~ N(0, 1/r), zero beyond the slot's rank
+            view = self.b[offsets[g] : offsets[g] + N * buckets[g]].view(N, int(buckets[g]))
+            view.mul_(1.0 / float(ranks[g]) ** 0.5)
+            view[:, int(ranks[g]) :] = 0
+        self.offsets_np, self.buckets_np = offsets, buckets
+        self.b_offsets = torch.tensor(offsets, dtype=torch.int64, device=device)
+        self.b_strides = torch.tensor(buckets, dtype=torch.int32, device=device)
+        self.ranks = torch.tensor(ranks, dtype=torch.int32, device=device)
+        self.scales = torch.tensor(scales, dtype=torch.float32, device=device)
         self.slice_offsets = torch.tensor(np.cumsum((0, *widths)), dtype=torch.int32, device=device)
-        self.z = torch.zeros(T_TOKENS, S * RANK, dtype=torch.bfloat16, device=device)
-        from loraforge_b200.ops.fused import workspace_floats
-
+        self.z = torch.zeros(tokens, S * cap, dtype=torch.bfloat16, device=device)
         self.workspace = torch.empty(
-            workspace_floats(T_TOKENS, K, S, RANK), dtype=torch.float32, device=device
+            workspace_floats(tokens, K, S, cap), dtype=torch.float32, device=device
         )
-        self.y = torch.zeros(T_TOKENS, N, dtype=torch.bfloat16, device=device)
+        self.y = torch.zeros(tokens, N, dtype=torch.bfloat16, device=device)
 
     def b_rows(self, g):
-        """Host copy of slot g's B rows [N, r] (for the CPU oracle)."""
-        n = self.N * RANK
-        return self.b_host[g * n : (g + 1) * n].view(self.N, RANK)
+        """Host copy of slot g's B rows [N, bucket] (for the CPU oracle)."""
+        off, bucket = int(self.offsets_np[g]), int(self.buckets_np[g])
+        return self.b_host[off : off + self.N * bucket].view(self.N, bucket)
 
     # Algorithmic bytes (the rank-r intermediate's round trip is not counted).
     def shrink_bytes(self, touched, t_active):
-        return t_active * self.K * 2 + touched * self.S * RANK * self.K * 2
+        return t_active * self.K * 2 + int(self.ranks_np[touched].sum()) * self.S * self.K * 2
 
     def expand_bytes(self, touched, t_active):
-        return touched * self.N * RANK * 2 + t_active * self.N * 2 * 2
+        return int(self.buckets_np[touched].sum()) * self.N * 2 + t_active * self.N * 2 * 2
 
-    def flops(self, t_active):
-        return t_active * 2 * RANK * (self.S * self.K + self.N)
+    def flops(self, slots):
+        r = self.ranks_np[slots[slots >= 0]]
+        return int((2 * r * (self.S * self.K + self.N)).sum())
 
 
 class Workload:
-    def __init__(self, device, seed):
+    def __init__(self, config, device, seed):
         import torch
 
         from loraforge_b200.ops.grouping import empty_routing
 
+        c = CONFIGS[config]
         gen = torch.Generator(device=device).manual_seed(seed)
         rng = np.random.default_rng(seed)
-        self.device = device
-        self.slots_np = zipf_slots(rng, T_TOKENS, N_SLOTS, ZIPF_S)
+        self.config, self.device, self.T, self.nslots = config, device, c["tokens"], c["slots"]
+        self.ranks_np, self.scales_np, self.slots_np = config_routing(config, rng)
         self.slots = torch.from_numpy(self.slots_np).to(device)
-        self.x_in = torch.randn(T_TOKENS, 4096, generator=gen, device=device).bfloat16()
-        self.x_down = torch.randn(T_TOKENS, 14336, generator=gen, device=device).bfloat16()
-        self.projections = [Projection(n, k, w, device, gen) for n, k, w in PROJECTIONS]
-        self.routing = empty_routing(T_TOKENS, device)
-        self.touched = int(len(np.unique(self.slots_np[self.slots_np >= 0])))
+        self.x = {}
+        for _, k, _ in c["projections"]:
+            if k not in self.x:
+                self.x[k] = torch.randn(self.T, k, generator=gen, device=device).bfloat16()
+        self.projections = [
+            Projection(n, k, w, self.ranks_np, self.scales_np, c["cap"], self.T, device, gen)
+            for n, k, w in c["projections"]
+        ]
+        self.routing = empty_routing(self.T, device)
+        self.touched = np.unique(self.slots_np[self.slots_np >= 0])
         self.t_active = int((self.slots_np >= 0).sum())
 
     def x_of(self, p):
-        return self.x_down if p.K == 14336 else self.x_in
+        return self.x[p.K]
 
     def bytes_per_step(self):
         return sum(
             p.shrink_bytes(self.touched, self.t_active) + p.expand_bytes(self.touched, self.t_active)
             for p in self.projections
-        ) + T_TOKENS * 4
+        ) + self.T * 4
 
     def flops_per_step(self):
-        return sum(p.flops(self.t_active) for p in self.projections)
+        return sum(p.flops(self.slots_np) for p in self.projections)
 
 
 def run_step(w, events=None):
-    """Grouping + LoRA shrink/expand of the three projections through the public API.
+    """Grouping + LoRA shrink/expand of every projection through the public API.
 
-    ``w.path == "fused"``: one lora_shrink_expand launch per projection;
-    ``"rows"``: row_shrink + row_expand per projection (the reference's operator pair).
-    ``events[i]`` = (start, mid, end) CUDA events around projection i's launches.
+    ``w.path == "fused"``: lora_shrink_expand per projection; ``"rows"``: row_shrink +
+    row_expand per projection (the reference's operator pair).  ``events[i]`` =
+    (start, mid, end) CUDA events around projection i's launches.
     """
     from loraforge_b200.ops import row_expand, row_shrink
     from loraforge_b200.ops.fused import lora_shrink_expand
     from loraforge_b200.ops.grouping import group_tokens
 
-    r = group_tokens(w.slots, N_SLOTS, chunk=16, out=w.routing)
+    r = group_tokens(w.slots, w.nslots, chunk=16, out=w.routing)
     routing = dict(
         segment_indptr=r.segment_indptr, segment_slots=r.segment_slots,
         token_indices=r.token_indices, segment_count=r.segment_count,
@@ -167,7 +236,7 @@ def run_step(w, events=None):
             if events is not None:
                 events[i][1].record()
         else:
-            row_shrink(w.x_of(p), p.a, p.z, w.slots, p.ranks, num_slices=p.S, max_rank=RANK)
+            row_shrink(w.x_of(p), p.a, p.z, w.slots, p.ranks, num_slices=p.S, max_rank=p.cap)
             if events is not None:
                 events[i][1].record()
             row_expand(p.z, p.b, p.y, **meta)
@@ -175,8 +244,8 @@ def run_step(w, events=None):
             events[i][2].record()
 
 
-def launches_per_step(path):
-    return 1 + 2 * len(PROJECTIONS)  # grouping + two kernels per projection
+def launches_per_step(w):
+    return 1 + 2 * len(w.projections)  # grouping + two kernels per projection
 
 
 # ----------------------------------------------------------------------------- clocks
@@ -287,15 +356,15 @@ def time_graph(w, steps, warmup, flush):
     del graph
     # Kernel breakdown: eager launches queued behind a device sleep so that host
     # launch latency never shows up between the events; L2 flushed before each step.
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in PROJECTIONS]
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in w.projections]
     kinds = ("fused",) if w.path == "fused" else ("shrink", "expand")
-    per_kernel = {f"{p[0]}.{k}": [] for p in PROJECTIONS for k in kinds}
+    per_kernel = {f"{p.name}.{k}": [] for p in w.projections for k in kinds}
     for _ in range(min(steps, 50)):
         flush.zero_()
         torch.cuda._sleep(4_000_000)
         run_step(w, events=ev)
         torch.cuda.synchronize()
-        for (name, _, _), (e0, e1, e2) in zip(PROJECTIONS, ev):
+        for name, (e0, e1, e2) in zip((p.name for p in w.projections), ev):
             if w.path == "fused":
                 per_kernel[f"{name}.fused"].append(e0.elapsed_time(e2))
             else:
@@ -308,16 +377,15 @@ def time_e2e(w, steps, warmup):
     """Public API with host buffers: H2D inputs, the step, D2H outputs, per step."""
     import torch
 
-    host_x_in = w.x_in.cpu().pin_memory()
-    host_x_down = w.x_down.cpu().pin_memory()
+    host_x = {k: v.cpu().pin_memory() for k, v in w.x.items()}
     host_slots = w.slots.cpu().pin_memory()
     host_out = [torch.empty(p.y.shape, dtype=p.y.dtype).pin_memory() for p in w.projections]
-    h2d = host_x_in.numel() * 2 + host_x_down.numel() * 2 + host_slots.numel() * 4
+    h2d = sum(t.numel() * 2 for t in host_x.values()) + host_slots.numel() * 4
     d2h = sum(t.numel() * 2 for t in host_out)
 
     def one():
-        w.x_in.copy_(host_x_in, non_blocking=True)
-        w.x_down.copy_(host_x_down, non_blocking=True)
+        for k, t in host_x.items():
+            w.x[k].copy_(t, non_blocking=True)
         w.slots.copy_(host_slots, non_blocking=True)
         run_step(w)
         for p, h in zip(w.projections, host_out):
@@ -344,34 +412,35 @@ def cpu_baseline(w, budget_s=15.0):
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     slots = w.slots_np
-    x_in = w.x_in.float().cpu()
-    x_down = w.x_down.float().cpu()
+    xs = {k: v.float().cpu() for k, v in w.x.items()}
     hosts = []
     for p in w.projections:
         p.b_host = p.b.cpu()
-        hosts.append((p, p.a.cpu()))
-    ranks = np.full(N_SLOTS, RANK)
-    scales = np.full(N_SLOTS, SCALE)
+        hosts.append((p, p.a.cpu(), p.slice_offsets.cpu().numpy()))
 
     def step():
-        for p, a_host in hosts:
-            x = x_down if p.K == 14336 else x_in
-            lora_delta_fp32(x, a_host, p.b_rows, slots, ranks, scales, p.slice_offsets.cpu().numpy())
+        for p, a_host, bounds in hosts:
+            lora_delta_fp32(xs[p.K], a_host, p.b_rows, slots, w.ranks_np, w.scales_np, bounds)
 
-    step()  # warm-up
+    t0 = time.perf_counter()
+    step()  # warm-up (also sizes the sample)
+    first = time.perf_counter() - t0
     times = []
     begin = time.perf_counter()
     while time.perf_counter() - begin < budget_s and len(times) < 50:
         t0 = time.perf_counter()
         step()
         times.append(time.perf_counter() - t0)
+        if first > budget_s:
+            break
     per_step = statistics.median(times)
     return {
-        "value": T_TOKENS / per_step,
+        "value": w.T / per_step,
         "unit": "tokens/s",
         "cores": threads,
         "kind": "port",
-        "sample": f"{len(times)} full steps (3 projections x {T_TOKENS} tokens), median",
+        "sample": f"{len(times)} full steps ({len(w.projections)} projections x {w.T} tokens), "
+        "median",
     }
 
 
@@ -418,12 +487,12 @@ def main():
     args = parse_args()
     import torch
 
+    c = CONFIGS[args.config]
     config = {
-        "workload": "config1: decode BGMV, Llama-3-8B qkv/gate_up/down, 256 tokens, "
-        "128 adapters r=16, Zipf(1.1)",
-        "tokens": T_TOKENS,
-        "adapters": N_SLOTS,
-        "rank": RANK,
+        "workload": c["workload"],
+        "tokens": c["tokens"],
+        "adapters": c["slots"],
+        "rank_capacity": c["cap"],
         "l2": "flushed before every timed step (256 MiB write, outside the step events)",
     }
     if args.impl == "reference":
@@ -431,7 +500,7 @@ def main():
     world, rank, local = init_distributed()
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    w = Workload(device, args.seed + rank)
+    w = Workload(args.config, device, args.seed + rank)
     w.path = args.path
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
     steps, warmup = args.steps, max(3, args.warmup)
@@ -441,7 +510,7 @@ def main():
     barrier(world)
     total_ms = max_over_ranks(sum(step_ms), world)
     ms_per_step = total_ms / steps
-    value = world * T_TOKENS * steps / (total_ms / 1e3)
+    value = world * w.T * steps / (total_ms / 1e3)
     peak, peak_kind = measured_peaks()
     dominant = max(per_kernel, key=per_kernel.get)
     name, kind = dominant.split(".")
@@ -453,7 +522,7 @@ def main():
     }[kind]
     achieved = alg / (per_kernel[dominant] * 1e-3) / 1e9
     result = {
-        "metric": "multi-LoRA shrink+expand tokens/s (decode, config 1)",
+        "metric": METRIC,
         "value": value,
         "unit": "tokens/s",
         "n_gpus": world,
@@ -464,7 +533,7 @@ def main():
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "bf16",
-        "data": "synthetic (seeded; BASELINE config 1 shapes and distributions)",
+        "data": f"synthetic (seeded; BASELINE config {args.config} shapes and distributions)",
         "config": config | {"parallelism": f"replicas{world}", "path": w.path},
         "hbm_gbs_step": w.bytes_per_step() / (ms_per_step * 1e-3) / 1e9,
         "bytes_per_step": w.bytes_per_step(),
@@ -480,14 +549,14 @@ def main():
             "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
             "traffic": None,
         },
-        "gpu_launches": launches_per_step(w.path) * steps,
+        "gpu_launches": launches_per_step(w) * steps,
         "clocks": clocks.record(),
     }
     if not args.no_e2e and not args.profile:
         e2e_ms, h2d, d2h = time_e2e(w, max(10, steps // 10), 3)
         e2e_ms = max_over_ranks(e2e_ms, world)
         result["e2e"] = {
-            "value": world * T_TOKENS / (e2e_ms * 1e-3),
+            "value": world * w.T / (e2e_ms * 1e-3),
             "unit": "tokens/s",
             "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h,
@@ -506,35 +575,27 @@ def main_reference(args, config):
     """CPU oracle port of the reference path on the host cores (rank 0 only)."""
     import torch
 
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
+    if int(os.environ.get("RANK", "0")) != 0:
         return
-    device = torch.device("cpu")
-    w = Workload.__new__(Workload)
-    gen = torch.Generator().manual_seed(args.seed)
-    rng = np.random.default_rng(args.seed)
-    w.slots_np = zipf_slots(rng, T_TOKENS, N_SLOTS, ZIPF_S)
-    w.x_in = torch.randn(T_TOKENS, 4096, generator=gen).bfloat16()
-    w.x_down = torch.randn(T_TOKENS, 14336, generator=gen).bfloat16()
-    w.projections = [_host_projection(n, k, wd, gen) for n, k, wd in PROJECTIONS]
+    w = Workload(args.config, torch.device("cpu"), args.seed)
     budget = max(10.0, min(120.0, 2.0 * (args.steps + args.warmup)))
     base = cpu_baseline(w, budget_s=budget)
     print(
         json.dumps(
             {
                 "impl": "reference",
-                "metric": "multi-LoRA shrink+expand tokens/s (decode, config 1)",
+                "metric": METRIC,
                 "value": base["value"],
                 "unit": "tokens/s",
                 "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
                 "steps": args.steps,
                 "warmup": args.warmup,
-                "ms_per_step": 1e3 * T_TOKENS / base["value"],
+                "ms_per_step": 1e3 * w.T / base["value"],
                 "higher_is_better": True,
                 "scaling": "weak",
                 "vs_baseline": None,
                 "dtype": "f32",
-                "data": "synthetic (seeded; BASELINE config 1 shapes and distributions)",
+                "data": f"synthetic (seeded; BASELINE config {args.config} shapes and distributions)",
                 "config": config | {"parallelism": "host cores"},
                 "cpu_baseline": base,
                 "e2e": {"value": base["value"], "unit": "tokens/s",
@@ -543,17 +604,6 @@ def main_reference(args, config):
         ),
         flush=True,
     )
-
-
-def _host_projection(name, k, widths, gen):
-    import torch
-
-    p = Projection.__new__(Projection)
-    p.name, p.K, p.widths, p.S, p.N = name, k, widths, len(widths), sum(widths)
-    p.a = (torch.randn(N_SLOTS, p.S * RANK, k, generator=gen) / k**0.5).bfloat16()
-    p.b = (torch.randn(N_SLOTS * p.N * RANK, generator=gen) / RANK**0.5).bfloat16()
-    p.slice_offsets = torch.tensor(np.cumsum((0, *widths)), dtype=torch.int32)
-    return p
 
 
 if __name__ == "__main__":
