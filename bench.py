@@ -150,7 +150,7 @@ class Projection:
         self.scales = torch.tensor(scales, dtype=torch.float32, device=device)
         self.slice_offsets = torch.tensor(np.cumsum((0, *widths)), dtype=torch.int32, device=device)
         self.z = torch.zeros(tokens, S * cap, dtype=torch.bfloat16, device=device)
-        self.workspace = torch.empty(
+        self.workspace = torch.zeros(
             workspace_floats(tokens, K, S, cap), dtype=torch.float32, device=device
         )
         self.y = torch.zeros(tokens, N, dtype=torch.bfloat16, device=device)

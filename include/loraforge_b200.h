@@ -161,7 +161,10 @@ int lf_vllm_expand(int32_t dtype, const float* v, const lf_slice_desc* slices,
  *   numerics 1 (reference): y[t, n] = bf16(y + bf16(scale_g * sum_k bf16(z) B_g[n, k]))
  * with k < min(r, b).  `workspace` is FP32 scratch of at least
  * lf_fused_workspace_floats(...) floats, 16-byte aligned, holding per-K-chunk
- * partial sums of z (added in chunk order, so results are deterministic; no atomics).
+ * partial sums of z (added in chunk order, so results are deterministic; no
+ * floating-point atomics), the FP32 z rows and one completion counter per segment.
+ * It must be zero-filled before its first use; every call leaves the counters at
+ * zero again, so one workspace serves any sequence of calls on one stream.
  * Requires width and x_stride multiples of 8, 16-byte aligned x/A/B, 8-byte aligned
  * y with y_stride a multiple of 4 and B regions at 8-element offsets.  Fused,
  * grouped form of the reference's two decode kernels (src/loraforge/ops/csrc/
@@ -195,9 +198,10 @@ int64_t lf_fused_workspace_floats(int64_t num_tokens, int64_t width, int32_t num
  * The first call on a device looks up the buffer's device address
  * (cudaGetSymbolAddress) with that device current; make that first call before any
  * stream capture.  All calls on a device share the buffer and it keeps the last call's
- * contents (every value a call reads is written earlier in the same call, so nothing
- * needs clearing); calls that overlap on the GPU (other streams, or graphs replayed
- * concurrently) race on it and must be serialised by the caller.
+ * contents: the buffer starts zero-filled and every call leaves its per-segment
+ * counters at zero, so each call finds them cleared; calls that overlap on the GPU
+ * (other streams, or graphs replayed concurrently) race on it and must be serialised
+ * by the caller.
  */
 int lf_fused_shrink_expand_noalloc(const void* x, int64_t x_stride, const void* a,
                                    const void* b, const int64_t* b_offsets,

@@ -2,12 +2,13 @@
 
 ``lora_shrink_expand`` takes the operands of ``row_shrink`` (x, packed A) and of
 ``row_expand`` (compact B store, per-slot metadata, routing tables) and computes
-``output += scale * B @ (A @ x)`` for every routed token in one call: a grouped
-shrink kernel (each adapter's A rows read once per segment, K split over a
-thread-block cluster) chained by programmatic dependent launch to a grouped expand
-kernel, with the rank-r intermediate kept in FP32.  It is the B200 form of the reference's two-kernel decode
-path (src/loraforge/ops/lora_rows.py:54-239 as driven by
-src/loraforge/integrations/_sglang_fleet.py:271-407).
+``output += scale * B @ (A @ x)`` for every routed token in one call: a persistent
+grouped shrink kernel (each adapter's A rows streamed once per segment, K split into
+chunks whose partial sums are reduced deterministically) chained by programmatic
+dependent launch to a persistent grouped expand kernel, both fed by bulk-copy
+pipelines, with the rank-r intermediate kept in FP32.  It is the B200 form of the
+reference's two-kernel decode path (src/loraforge/ops/lora_rows.py:54-239 as driven
+by src/loraforge/integrations/_sglang_fleet.py:271-407).
 
 ``numerics="fp32"`` (default) keeps z in FP32 and rounds the output once;
 ``numerics="reference"`` reproduces the retained-rank operators' contract (BF16 z,
@@ -57,8 +58,11 @@ def lora_shrink_expand(
     (``group_tokens(..., chunk=16)``).  Slot -1 / rank-0 segments leave output
     unchanged.  ``workspace`` is an optional FP32 buffer of at least
     ``workspace_floats(tokens, width, num_slices, capacity)`` elements for the
-    shrink's partial sums (allocated per call when omitted; pass one to keep a
-    captured graph allocation-free).
+    shrink's partial sums, the FP32 z rows and per-segment completion counters
+    (allocated per call when omitted; pass one to keep a captured graph
+    allocation-free).  A caller-owned workspace must be zero-filled before its
+    first use (``torch.zeros``); every call leaves its counters at zero again, so
+    one workspace serves any sequence of calls on one stream.
     """
     import torch
 
@@ -112,7 +116,7 @@ def lora_shrink_expand(
     capacity = a.shape[1] // num_slices
     need = _native.fused_workspace_floats(x.shape[0], x.shape[1], num_slices, capacity)
     if workspace is None:
-        workspace = torch.empty(need, dtype=torch.float32, device=x.device)
+        workspace = torch.zeros(need, dtype=torch.float32, device=x.device)
     if (
         not isinstance(workspace, torch.Tensor)
         or workspace.dtype != torch.float32
