@@ -164,7 +164,9 @@ int lf_vllm_expand(int32_t dtype, const float* v, const lf_slice_desc* slices,
  * partial sums of z (added in chunk order, so results are deterministic; no
  * floating-point atomics), the FP32 z rows and one completion counter per segment.
  * It must be zero-filled before its first use; every call leaves the counters at
- * zero again, so one workspace serves any sequence of calls on one stream.
+ * zero again, so one workspace serves any sequence of calls with the same num_tokens,
+ * width, num_slices and capacity on one stream (the counters' offset depends on them:
+ * zero the workspace again before calls with other sizes).
  * Requires width and x_stride multiples of 8, 16-byte aligned x/A/B, 8-byte aligned
  * y with y_stride a multiple of 4 and B regions at 8-element offsets.  Fused,
  * grouped form of the reference's two decode kernels (src/loraforge/ops/csrc/
@@ -192,16 +194,18 @@ int64_t lf_fused_workspace_floats(int64_t num_tokens, int64_t width, int32_t num
  * cudaMalloc calls, and foreign-language hosts (cgo, JNI, N-API) that have no access
  * to the framework's caching allocator and must not create untracked allocations.
  * This entry point allocates nothing (no cudaMalloc, cudaFree or allocating library
- * call): its scratch is a 16 MiB array (4 Mi floats) compiled into the library, which
- * every GPU that loads the library holds until the process exits.  Sizes whose
- * lf_fused_workspace_floats(...) exceeds 4 Mi floats are rejected with LF_E_INVALID.
+ * call): its scratch is a 16 MiB array (4 Mi floats) compiled into the library plus a
+ * 64 KiB array of per-segment counters at fixed positions, which every GPU that loads
+ * the library holds until the process exits.  Sizes whose
+ * lf_fused_workspace_floats(...) exceeds 4 Mi floats, or more than 16384 tokens, are
+ * rejected with LF_E_INVALID.
  * The first call on a device looks up the buffer's device address
  * (cudaGetSymbolAddress) with that device current; make that first call before any
  * stream capture.  All calls on a device share the buffer and it keeps the last call's
- * contents: the buffer starts zero-filled and every call leaves its per-segment
- * counters at zero, so each call finds them cleared; calls that overlap on the GPU
- * (other streams, or graphs replayed concurrently) race on it and must be serialised
- * by the caller.
+ * contents: the counters start zero-filled and every call leaves them at zero, so calls
+ * of any sizes may follow one another; calls that overlap on the GPU (other streams,
+ * or graphs replayed concurrently) race on the buffers and must be serialised by the
+ * caller.
  */
 int lf_fused_shrink_expand_noalloc(const void* x, int64_t x_stride, const void* a,
                                    const void* b, const int64_t* b_offsets,

@@ -918,6 +918,25 @@ extern "C" int64_t lf_fused_workspace_floats(int64_t num_tokens, int64_t width,
   return scratch_floats(num_tokens, shrink_config(width, num_slices, capacity));
 }
 
+namespace {
+// One call's scratch: FP32 partials and z rows (every value read is written earlier in
+// the same call) and one completion counter per segment (zero before the first call;
+// every call leaves the counters it used at zero).
+struct Scratch {
+  float* data;
+  int* counters;
+};
+
+int fused_launch(const void* x, int64_t x_stride, const void* a, const void* b,
+                 const int64_t* b_offsets, const int32_t* b_strides, void* y, int64_t y_stride,
+                 const int32_t* segment_indptr, const int32_t* segment_slots,
+                 const int32_t* token_indices, const int32_t* ranks, const float* scales,
+                 const int32_t* slice_offsets, const int32_t* segment_count, const Scratch& scratch,
+                 int64_t num_tokens, int64_t width, int32_t out_width, int32_t num_slices,
+                 int32_t capacity, int32_t num_slots, int32_t max_segments, int32_t numerics,
+                 void* stream);
+}  // namespace
+
 extern "C" int lf_fused_shrink_expand(
     const void* x, int64_t x_stride, const void* a, const void* b, const int64_t* b_offsets,
     const int32_t* b_strides, void* y, int64_t y_stride, const int32_t* segment_indptr,
@@ -926,6 +945,33 @@ extern "C" int lf_fused_shrink_expand(
     float* workspace, int64_t workspace_floats, int64_t num_tokens, int64_t width,
     int32_t out_width, int32_t num_slices, int32_t capacity, int32_t num_slots,
     int32_t max_segments, int32_t numerics, void* stream) {
+  if (num_tokens < 0 || num_tokens >= (int64_t(1) << 31) || width < 1 || width >= (int64_t(1) << 31))
+    return fail(LF_E_INVALID, "fused_shrink_expand: invalid token count or width");
+  if (num_slices < 1 || num_slices > kMaxSlices || capacity < 1)
+    return fail(LF_E_INVALID, "fused_shrink_expand: invalid slices or capacity");
+  const ShrinkConfig sc = shrink_config(width, num_slices, capacity);
+  const int64_t need = scratch_floats(num_tokens, sc);
+  if (!workspace || workspace_floats < need || (reinterpret_cast<uintptr_t>(workspace) & 15))
+    return fail(LF_E_INVALID, "fused_shrink_expand: workspace too small or not 16-byte aligned "
+                              "(see lf_fused_workspace_floats)");
+  const int64_t T = num_tokens > 0 ? num_tokens : 1;
+  const Scratch scratch{
+      workspace, reinterpret_cast<int*>(workspace + (int64_t(sc.nchunks) + 1) * T * sc.rstride)};
+  return fused_launch(x, x_stride, a, b, b_offsets, b_strides, y, y_stride, segment_indptr,
+                      segment_slots, token_indices, ranks, scales, slice_offsets, segment_count,
+                      scratch, num_tokens, width, out_width, num_slices, capacity, num_slots,
+                      max_segments, numerics, stream);
+}
+
+namespace {
+int fused_launch(const void* x, int64_t x_stride, const void* a, const void* b,
+                 const int64_t* b_offsets, const int32_t* b_strides, void* y, int64_t y_stride,
+                 const int32_t* segment_indptr, const int32_t* segment_slots,
+                 const int32_t* token_indices, const int32_t* ranks, const float* scales,
+                 const int32_t* slice_offsets, const int32_t* segment_count, const Scratch& scratch,
+                 int64_t num_tokens, int64_t width, int32_t out_width, int32_t num_slices,
+                 int32_t capacity, int32_t num_slots, int32_t max_segments, int32_t numerics,
+                 void* stream) {
   if (num_tokens < 0 || num_tokens >= (int64_t(1) << 31) || width < 1 || width >= (int64_t(1) << 31))
     return fail(LF_E_INVALID, "fused_shrink_expand: invalid token count or width");
   if (out_width < 1 || num_slices < 1 || num_slices > kMaxSlices || capacity < 1 || num_slots < 1)
@@ -938,10 +984,6 @@ extern "C" int lf_fused_shrink_expand(
     return fail(LF_E_INVALID, "fused_shrink_expand: numerics must be 0 (fp32) or 1 (reference)");
   if (max_segments < 0) return fail(LF_E_INVALID, "fused_shrink_expand: negative segment capacity");
   const ShrinkConfig sc = shrink_config(width, num_slices, capacity);
-  const int64_t need = scratch_floats(num_tokens, sc);
-  if (!workspace || workspace_floats < need || (reinterpret_cast<uintptr_t>(workspace) & 15))
-    return fail(LF_E_INVALID, "fused_shrink_expand: workspace too small or not 16-byte aligned "
-                              "(see lf_fused_workspace_floats)");
   if (num_tokens == 0 || max_segments == 0) return LF_OK;
   const bool staged = out_width % 8 == 0 && y_stride % 8 == 0 &&
                       (reinterpret_cast<uintptr_t>(y) & 15) == 0;
@@ -950,9 +992,8 @@ extern "C" int lf_fused_shrink_expand(
   Params p{static_cast<const uint16_t*>(x), x_stride, static_cast<const uint16_t*>(a),
            static_cast<const uint16_t*>(b), b_offsets, b_strides, static_cast<uint16_t*>(y),
            y_stride, segment_indptr, segment_slots, token_indices, ranks, scales, slice_offsets,
-           segment_count, workspace, workspace + int64_t(sc.nchunks) * T * sc.rstride,
-           reinterpret_cast<int*>(workspace + (int64_t(sc.nchunks) + 1) * T * sc.rstride),
-           int(T), int(width), out_width, num_slices, capacity, num_slots, max_segments,
+           segment_count, scratch.data, scratch.data + int64_t(sc.nchunks) * T * sc.rstride,
+           scratch.counters, int(T), int(width), out_width, num_slices, capacity, num_slots, max_segments,
            sc.rstride, sc.kc, sc.nchunks, sc.stages, sc.stage_bytes, 0};
   {
     // A as a 2-D tensor [num_slots*S*cap rows, K columns] for the shrink's TMA boxes.
@@ -1000,6 +1041,7 @@ extern "C" int lf_fused_shrink_expand(
   if (int rc = ensure_smem(kernel, ec.smem, flags[numerics * 2 + (staged ? 1 : 0)])) return rc;
   return launch_pdl(kernel, grid, ec.smem, s, p, "fused_shrink_expand (expand)");
 }
+}  // namespace
 
 extern "C" int lf_device_wait_timeouts(int32_t* count, int32_t reset) {
   unsigned int value = 0;
@@ -1016,16 +1058,21 @@ extern "C" int lf_device_wait_timeouts(int32_t* count, int32_t reset) {
 
 // ------------------------------------------------------------------ allocation-free entry
 // lf_fused_shrink_expand_noalloc runs the same two kernels as lf_fused_shrink_expand
-// but takes its scratch from a fixed buffer compiled into this library, for callers
+// but takes its scratch from fixed buffers compiled into this library, for callers
 // that are not allowed to allocate device memory themselves.
 namespace {
-// 4 Mi floats (16 MiB).  A static __device__ array is created on every GPU that loads
-// this library, zero-filled, and lives until the process exits.
+// 4 Mi floats (16 MiB) of partial sums and z rows, and one completion counter for each
+// of up to kNoAllocTokens segments at a fixed position (so calls of different sizes
+// may follow one another).  Static __device__ arrays are created on every GPU that
+// loads this library, zero-filled, and live until the process exits.
 constexpr int64_t kNoAllocScratchFloats = int64_t(4) << 20;
+constexpr int64_t kNoAllocTokens = 16384;
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+static __device__ __align__(256) int g_noalloc_counters[kNoAllocTokens];
 
 std::mutex g_noalloc_mutex;
-float* g_noalloc_address[64] = {};  // device address of the buffer, per device
+float* g_noalloc_address[64] = {};  // device address of the data buffer, per device
+int* g_noalloc_counters_address[64] = {};
 }  // namespace
 
 extern "C" int lf_fused_shrink_expand_noalloc(
@@ -1037,37 +1084,41 @@ extern "C" int lf_fused_shrink_expand_noalloc(
     int32_t num_slots, int32_t max_segments, int32_t numerics, void* stream) {
   const int64_t need = lf_fused_workspace_floats(num_tokens, width, num_slices, capacity);
   if (need < 0) return fail(LF_E_INVALID, "fused_shrink_expand_noalloc: invalid sizes");
-  if (need > kNoAllocScratchFloats) {
+  if (need > kNoAllocScratchFloats || num_tokens > kNoAllocTokens) {
     last_error() = "fused_shrink_expand_noalloc: these sizes need " + std::to_string(need) +
-                   " floats of scratch, more than the built-in " +
-                   std::to_string(kNoAllocScratchFloats) +
-                   "-float (16 MiB) buffer; use lf_fused_shrink_expand with a workspace";
+                   " floats of scratch for " + std::to_string(num_tokens) +
+                   " tokens, more than the built-in " + std::to_string(kNoAllocScratchFloats) +
+                   "-float (16 MiB) buffer or " + std::to_string(kNoAllocTokens) +
+                   " tokens; use lf_fused_shrink_expand with a workspace";
     return LF_E_INVALID;
   }
   int device = 0;
   if (cudaGetDevice(&device) != cudaSuccess) return check_launch("fused_shrink_expand_noalloc");
   if (device < 0 || device >= 64)
     return fail(LF_E_UNSUPPORTED, "fused_shrink_expand_noalloc: device index above 63");
-  float* scratch = nullptr;
+  Scratch scratch{};
   {
-    // First call on a device: look up the buffer's device address with that device
-    // current.  The host-side name g_noalloc_scratch is not a device address.
+    // First call on a device: look up the buffers' device addresses with that device
+    // current.  The host-side names g_noalloc_scratch / g_noalloc_counters are not
+    // device addresses.
     std::lock_guard<std::mutex> lock(g_noalloc_mutex);
     if (!g_noalloc_address[device]) {
       void* address = nullptr;
-      const cudaError_t err = cudaGetSymbolAddress(&address, g_noalloc_scratch);
-      if (err != cudaSuccess || !address) {
+      void* counters = nullptr;
+      cudaError_t err = cudaGetSymbolAddress(&address, g_noalloc_scratch);
+      if (err == cudaSuccess) err = cudaGetSymbolAddress(&counters, g_noalloc_counters);
+      if (err != cudaSuccess || !address || !counters) {
         last_error() = std::string("fused_shrink_expand_noalloc: cudaGetSymbolAddress: ") +
                        cudaGetErrorString(err);
         return LF_E_CUDA;
       }
       g_noalloc_address[device] = static_cast<float*>(address);
+      g_noalloc_counters_address[device] = static_cast<int*>(counters);
     }
-    scratch = g_noalloc_address[device];
+    scratch = Scratch{g_noalloc_address[device], g_noalloc_counters_address[device]};
   }
-  return lf_fused_shrink_expand(x, x_stride, a, b, b_offsets, b_strides, y, y_stride,
-                                segment_indptr, segment_slots, token_indices, ranks, scales,
-                                slice_offsets, segment_count, scratch, kNoAllocScratchFloats,
-                                num_tokens, width, out_width, num_slices, capacity, num_slots,
-                                max_segments, numerics, stream);
+  return fused_launch(x, x_stride, a, b, b_offsets, b_strides, y, y_stride, segment_indptr,
+                      segment_slots, token_indices, ranks, scales, slice_offsets, segment_count,
+                      scratch, num_tokens, width, out_width, num_slices, capacity, num_slots,
+                      max_segments, numerics, stream);
 }

@@ -66,10 +66,16 @@ def call_noalloc(x, a, b, out, meta, S, rank, numerics=0):
 @pytest.mark.parametrize("numerics", ["fp32", "reference"])
 def test_matches_workspace_entry_point_on_consecutive_calls(numerics):
     code = {"fp32": 0, "reference": 1}[numerics]
-    # Two different problems back to back: the second call starts from the first
-    # call's leftovers in the shared buffer.
-    for seed, widths in ((1, (4096, 1024, 1024)), (2, (14336, 14336))):
-        x, a, b, base, meta, S, rank = make_case(seed, widths=widths)
+    # Different problems back to back (other slice counts, widths and token counts):
+    # every call starts from the previous call's leftovers in the shared buffers.
+    cases = (
+        (1, 96, 4096, (4096, 1024, 1024)),
+        (2, 96, 4096, (14336, 14336)),
+        (3, 40, 14336, (4096,)),
+        (4, 160, 4096, (4096, 1024, 1024)),
+    )
+    for seed, tokens, k, widths in cases:
+        x, a, b, base, meta, S, rank = make_case(seed, tokens=tokens, k=k, widths=widths)
         expected = base.clone()
         lora_shrink_expand(x, a, b, expected, **meta, num_slices=S, numerics=numerics)
         got = base.clone()
