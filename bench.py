@@ -44,6 +44,12 @@ import numpy as np
 ROOT = Path(__file__).resolve().parent
 METRIC = "multi-LoRA shrink+expand tokens/s"
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of the dominant
+# call, from one ncu capture per (config, path, call); see profiles/ for the commands.
+TRAFFIC = {
+    (1, "fused", "gate_up_proj.fused"): (19.430144 + 75.358720 + 3.842816) * 1e6,
+}
+
 
 def parse_args():
     p = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
@@ -547,7 +553,7 @@ def main():
             "unit": "GB/s",
             "frac": achieved / peak,
             "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
-            "traffic": None,
+            "traffic": TRAFFIC.get((args.config, w.path, dominant)),
         },
         "gpu_launches": launches_per_step(w) * steps,
         "clocks": clocks.record(),
