@@ -103,7 +103,7 @@ CONFIGS = {
     3: dict(
         workload="config3: prefill SGMV, 8192 tokens in 32 geometric segments (mean 256), "
         "64 adapters r=64, 5120->5120",
-        tokens=8192, slots=64, cap=64, projections=(("proj", 5120, (5120,)),),
+        tokens=8192, slots=64, cap=64, projections=(("proj", 5120, (5120,)),), prefill=True,
     ),
 }
 
@@ -132,10 +132,10 @@ def config_routing(config, rng):
 class Projection:
     """One LoRA-augmented projection: packed A, compact B store, per-slot metadata."""
 
-    def __init__(self, name, k, widths, ranks, scales, cap, tokens, device, gen):
+    def __init__(self, name, k, widths, ranks, scales, cap, tokens, device, gen, prefill=False):
         import torch
 
-        from loraforge_b200.ops.fused import workspace_floats
+        from loraforge_b200.ops.fused import prefill_workspace_floats, workspace_floats
 
         self.name, self.K, self.widths = name, k, widths
         self.S, self.N = len(widths), sum(widths)
@@ -156,9 +156,8 @@ class Projection:
         self.scales = torch.tensor(scales, dtype=torch.float32, device=device)
         self.slice_offsets = torch.tensor(np.cumsum((0, *widths)), dtype=torch.int32, device=device)
         self.z = torch.zeros(tokens, S * cap, dtype=torch.bfloat16, device=device)
-        self.workspace = torch.zeros(
-            workspace_floats(tokens, K, S, cap), dtype=torch.float32, device=device
-        )
+        sizer = prefill_workspace_floats if prefill else workspace_floats
+        self.workspace = torch.zeros(sizer(tokens, K, S, cap), dtype=torch.float32, device=device)
         self.y = torch.zeros(tokens, N, dtype=torch.bfloat16, device=device)
 
     def b_rows(self, g):
@@ -188,6 +187,7 @@ class Workload:
         gen = torch.Generator(device=device).manual_seed(seed)
         rng = np.random.default_rng(seed)
         self.config, self.device, self.T, self.nslots = config, device, c["tokens"], c["slots"]
+        self.prefill = c.get("prefill", False)
         self.ranks_np, self.scales_np, self.slots_np = config_routing(config, rng)
         self.slots = torch.from_numpy(self.slots_np).to(device)
         self.x = {}
@@ -195,7 +195,8 @@ class Workload:
             if k not in self.x:
                 self.x[k] = torch.randn(self.T, k, generator=gen, device=device).bfloat16()
         self.projections = [
-            Projection(n, k, w, self.ranks_np, self.scales_np, c["cap"], self.T, device, gen)
+            Projection(n, k, w, self.ranks_np, self.scales_np, c["cap"], self.T, device, gen,
+                       c.get("prefill", False))
             for n, k, w in c["projections"]
         ]
         self.routing = empty_routing(self.T, device)
@@ -218,15 +219,19 @@ class Workload:
 def run_step(w, events=None):
     """Grouping + LoRA shrink/expand of every projection through the public API.
 
-    ``w.path == "fused"``: lora_shrink_expand per projection; ``"rows"``: row_shrink +
-    row_expand per projection (the reference's operator pair).  ``events[i]`` =
-    (start, mid, end) CUDA events around projection i's launches.
+    ``w.path == "fused"``: lora_shrink_expand per projection (prefill configs:
+    lora_shrink_expand_prefill over segments of up to 128 tokens, tcgen05 tiles for the
+    segments of 16 or more); ``"rows"``: row_shrink + row_expand per projection (the
+    reference's operator pair).  ``events[i]`` = (start, mid, end) CUDA events around
+    projection i's launches.
     """
     from loraforge_b200.ops import row_expand, row_shrink
-    from loraforge_b200.ops.fused import lora_shrink_expand
+    from loraforge_b200.ops.fused import lora_shrink_expand, lora_shrink_expand_prefill
     from loraforge_b200.ops.grouping import group_tokens
 
-    r = group_tokens(w.slots, w.nslots, chunk=16, out=w.routing)
+    prefill = w.prefill and w.path == "fused"
+    fused_op = lora_shrink_expand_prefill if prefill else lora_shrink_expand
+    r = group_tokens(w.slots, w.nslots, chunk=128 if prefill else 16, out=w.routing)
     routing = dict(
         segment_indptr=r.segment_indptr, segment_slots=r.segment_slots,
         token_indices=r.token_indices, segment_count=r.segment_count,
@@ -237,8 +242,7 @@ def run_step(w, events=None):
         if events is not None:
             events[i][0].record()
         if w.path == "fused":
-            lora_shrink_expand(w.x_of(p), p.a, p.b, p.y, **meta, num_slices=p.S,
-                               workspace=p.workspace)
+            fused_op(w.x_of(p), p.a, p.b, p.y, **meta, num_slices=p.S, workspace=p.workspace)
             if events is not None:
                 events[i][1].record()
         else:

@@ -183,6 +183,34 @@ int lf_fused_shrink_expand(const void* x, int64_t x_stride, const void* a, const
                            int32_t capacity, int32_t num_slots, int32_t max_segments,
                            int32_t numerics, void* stream);
 
+/*
+ * Grouped (SGMV) shrink -> expand for prefill batches: the arguments and numerics of
+ * lf_fused_shrink_expand, with segments of up to 128 tokens (group_tokens chunk 128).
+ * Segments of 16..128 tokens run on the tcgen05 tensor cores with TMEM accumulators
+ * (M = 128 tokens per tile; shrink N = S*r rounded up to 16, K split in parts of 1024 whose
+ * FP32 partials are added in order; expand N = 256 output columns, K = 64 zero-padded
+ * rank); segments of fewer than 16 tokens run on the decode kernels of
+ * lf_fused_shrink_expand in the same call.  `workspace` holds at least
+ * lf_sgmv_prefill_workspace_floats(...) floats, 16-byte aligned, zero-filled before its
+ * first use (reused as for lf_fused_shrink_expand).  Replaces the prefill path of the
+ * reference: the rank-aware SGMV shrink (src/loraforge/integrations/_sglang_rank_aware.py:
+ * 14-171) and the chunked SGMV expand it pairs with (SGLang's
+ * chunked_sgmv_lora_expand_forward, called at src/loraforge/integrations/
+ * _sglang_fleet.py:310-313 and :375-383).
+ */
+int lf_sgmv_prefill(const void* x, int64_t x_stride, const void* a, const void* b,
+                    const int64_t* b_offsets, const int32_t* b_strides, void* y, int64_t y_stride,
+                    const int32_t* segment_indptr, const int32_t* segment_slots,
+                    const int32_t* token_indices, const int32_t* ranks, const float* scales,
+                    const int32_t* slice_offsets, const int32_t* segment_count, float* workspace,
+                    int64_t workspace_floats, int64_t num_tokens, int64_t width, int32_t out_width,
+                    int32_t num_slices, int32_t capacity, int32_t num_slots, int32_t max_segments,
+                    int32_t numerics, void* stream);
+
+/* Workspace floats lf_sgmv_prefill needs for these sizes (-1 if invalid). */
+int64_t lf_sgmv_prefill_workspace_floats(int64_t num_tokens, int64_t width, int32_t num_slices,
+                                         int32_t capacity);
+
 /* Workspace floats lf_fused_shrink_expand needs for these sizes (-1 if invalid). */
 int64_t lf_fused_workspace_floats(int64_t num_tokens, int64_t width, int32_t num_slices,
                                   int32_t capacity);

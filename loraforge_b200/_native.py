@@ -52,6 +52,10 @@ SIGNATURES = {
         _p, _i64, _p, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _i64,
         _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _p,
     ],
+    "lf_sgmv_prefill": [
+        _p, _i64, _p, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _i64,
+        _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _p,
+    ],
     "lf_fused_shrink_expand_noalloc": [
         _p, _i64, _p, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _p,
         _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _p,
@@ -65,7 +69,8 @@ _lib = None
 
 def exported_symbols() -> tuple[str, ...]:
     """Every symbol the header declares (checked by the CPU test suite)."""
-    return ("lf_version", "lf_last_error_string", "lf_fused_workspace_floats", *SIGNATURES)
+    return ("lf_version", "lf_last_error_string", "lf_fused_workspace_floats",
+            "lf_sgmv_prefill_workspace_floats", *SIGNATURES)
 
 
 def library() -> ctypes.CDLL:
@@ -89,8 +94,9 @@ def library() -> ctypes.CDLL:
                 fn = getattr(lib, name)
                 fn.restype = ctypes.c_int
                 fn.argtypes = args
-            lib.lf_fused_workspace_floats.restype = ctypes.c_int64
-            lib.lf_fused_workspace_floats.argtypes = [_i64, _i64, _i32, _i32]
+            for sizer in ("lf_fused_workspace_floats", "lf_sgmv_prefill_workspace_floats"):
+                getattr(lib, sizer).restype = ctypes.c_int64
+                getattr(lib, sizer).argtypes = [_i64, _i64, _i32, _i32]
             _lib = lib
     return _lib
 
@@ -109,6 +115,14 @@ def fused_workspace_floats(num_tokens: int, width: int, num_slices: int, capacit
     n = library().lf_fused_workspace_floats(num_tokens, width, num_slices, capacity)
     if n < 0:
         raise ValueError("invalid sizes for the fused workspace")
+    return n
+
+
+def prefill_workspace_floats(num_tokens: int, width: int, num_slices: int, capacity: int) -> int:
+    """FP32 workspace size of lf_sgmv_prefill for these sizes."""
+    n = library().lf_sgmv_prefill_workspace_floats(num_tokens, width, num_slices, capacity)
+    if n < 0:
+        raise ValueError("invalid sizes for the prefill workspace")
     return n
 
 

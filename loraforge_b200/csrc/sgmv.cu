@@ -48,6 +48,7 @@
 #include <string>
 
 #include "launch.cuh"
+#include "sgmv.cuh"
 #include "tma.cuh"
 
 namespace lfb {
@@ -92,7 +93,7 @@ struct Params {
   int rstride;  // row stride of partial / zfinal: S*min(cap, 64) rounded up to 8
   int kc, nchunks;
   int stages, stage_bytes;  // of the kernel being launched
-  int unused;
+  int max_tokens;           // longer segments are left to the prefill (tcgen05) kernels
   CUtensorMap tmap_a;  // A as 2-D [slots*S*cap rows, K], boxes of 8 rows x min(kc, 256)
 };
 
@@ -144,7 +145,7 @@ __device__ __forceinline__ Seg load_segment_warp(const Params& p, int seg, int l
   s.pos0 = lo;
   s.n = hi - lo;
   s.g = p.seg_slots[seg];
-  bool ok = lo >= 0 && hi <= p.T && s.n >= 1 && s.n <= kSeg && s.g >= 0 && s.g < p.num_slots;
+  bool ok = lo >= 0 && hi <= p.T && s.n >= 1 && s.n <= p.max_tokens && s.g >= 0 && s.g < p.num_slots;
   if (ok) {
     s.r = p.ranks[s.g];
     s.bucket = p.b_strides[s.g];
@@ -918,24 +919,18 @@ extern "C" int64_t lf_fused_workspace_floats(int64_t num_tokens, int64_t width,
   return scratch_floats(num_tokens, shrink_config(width, num_slices, capacity));
 }
 
-namespace {
-// One call's scratch: FP32 partials and z rows (every value read is written earlier in
-// the same call) and one completion counter per segment (zero before the first call;
-// every call leaves the counters it used at zero).
-struct Scratch {
-  float* data;
-  int* counters;
-};
+namespace lfb {
+int64_t decode_scratch_floats(int64_t num_tokens, int64_t width, int num_slices, int capacity) {
+  return scratch_floats(num_tokens, shrink_config(width, num_slices, capacity));
+}
 
-int fused_launch(const void* x, int64_t x_stride, const void* a, const void* b,
-                 const int64_t* b_offsets, const int32_t* b_strides, void* y, int64_t y_stride,
-                 const int32_t* segment_indptr, const int32_t* segment_slots,
-                 const int32_t* token_indices, const int32_t* ranks, const float* scales,
-                 const int32_t* slice_offsets, const int32_t* segment_count, const Scratch& scratch,
-                 int64_t num_tokens, int64_t width, int32_t out_width, int32_t num_slices,
-                 int32_t capacity, int32_t num_slots, int32_t max_segments, int32_t numerics,
-                 void* stream);
-}  // namespace
+Scratch decode_scratch(float* region, int64_t num_tokens, int64_t width, int num_slices,
+                       int capacity) {
+  const ShrinkConfig sc = shrink_config(width, num_slices, capacity);
+  const int64_t T = num_tokens > 0 ? num_tokens : 1;
+  return Scratch{region, reinterpret_cast<int*>(region + (int64_t(sc.nchunks) + 1) * T * sc.rstride)};
+}
+}  // namespace lfb
 
 extern "C" int lf_fused_shrink_expand(
     const void* x, int64_t x_stride, const void* a, const void* b, const int64_t* b_offsets,
@@ -954,16 +949,14 @@ extern "C" int lf_fused_shrink_expand(
   if (!workspace || workspace_floats < need || (reinterpret_cast<uintptr_t>(workspace) & 15))
     return fail(LF_E_INVALID, "fused_shrink_expand: workspace too small or not 16-byte aligned "
                               "(see lf_fused_workspace_floats)");
-  const int64_t T = num_tokens > 0 ? num_tokens : 1;
-  const Scratch scratch{
-      workspace, reinterpret_cast<int*>(workspace + (int64_t(sc.nchunks) + 1) * T * sc.rstride)};
+  const Scratch scratch = decode_scratch(workspace, num_tokens, width, num_slices, capacity);
   return fused_launch(x, x_stride, a, b, b_offsets, b_strides, y, y_stride, segment_indptr,
                       segment_slots, token_indices, ranks, scales, slice_offsets, segment_count,
                       scratch, num_tokens, width, out_width, num_slices, capacity, num_slots,
-                      max_segments, numerics, stream);
+                      max_segments, numerics, kSeg, stream);
 }
 
-namespace {
+namespace lfb {
 int fused_launch(const void* x, int64_t x_stride, const void* a, const void* b,
                  const int64_t* b_offsets, const int32_t* b_strides, void* y, int64_t y_stride,
                  const int32_t* segment_indptr, const int32_t* segment_slots,
@@ -971,7 +964,7 @@ int fused_launch(const void* x, int64_t x_stride, const void* a, const void* b,
                  const int32_t* slice_offsets, const int32_t* segment_count, const Scratch& scratch,
                  int64_t num_tokens, int64_t width, int32_t out_width, int32_t num_slices,
                  int32_t capacity, int32_t num_slots, int32_t max_segments, int32_t numerics,
-                 void* stream) {
+                 int max_tokens, void* stream) {
   if (num_tokens < 0 || num_tokens >= (int64_t(1) << 31) || width < 1 || width >= (int64_t(1) << 31))
     return fail(LF_E_INVALID, "fused_shrink_expand: invalid token count or width");
   if (out_width < 1 || num_slices < 1 || num_slices > kMaxSlices || capacity < 1 || num_slots < 1)
@@ -994,7 +987,7 @@ int fused_launch(const void* x, int64_t x_stride, const void* a, const void* b,
            y_stride, segment_indptr, segment_slots, token_indices, ranks, scales, slice_offsets,
            segment_count, scratch.data, scratch.data + int64_t(sc.nchunks) * T * sc.rstride,
            scratch.counters, int(T), int(width), out_width, num_slices, capacity, num_slots, max_segments,
-           sc.rstride, sc.kc, sc.nchunks, sc.stages, sc.stage_bytes, 0};
+           sc.rstride, sc.kc, sc.nchunks, sc.stages, sc.stage_bytes, max_tokens};
   {
     // A as a 2-D tensor [num_slots*S*cap rows, K columns] for the shrink's TMA boxes.
     const PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
@@ -1041,13 +1034,15 @@ int fused_launch(const void* x, int64_t x_stride, const void* a, const void* b,
   if (int rc = ensure_smem(kernel, ec.smem, flags[numerics * 2 + (staged ? 1 : 0)])) return rc;
   return launch_pdl(kernel, grid, ec.smem, s, p, "fused_shrink_expand (expand)");
 }
-}  // namespace
+}  // namespace lfb
 
 extern "C" int lf_device_wait_timeouts(int32_t* count, int32_t reset) {
   unsigned int value = 0;
   if (cudaMemcpyFromSymbol(&value, g_lf_wait_timeouts, sizeof(value)) != cudaSuccess)
     return check_launch("device_wait_timeouts");
-  if (count) *count = int32_t(value);
+  unsigned int prefill = 0;
+  if (int rc = prefill_wait_timeouts(&prefill, reset)) return rc;
+  if (count) *count = int32_t(value + prefill);
   if (reset) {
     const unsigned int zero = 0;
     if (cudaMemcpyToSymbol(g_lf_wait_timeouts, &zero, sizeof(zero)) != cudaSuccess)
@@ -1120,5 +1115,5 @@ extern "C" int lf_fused_shrink_expand_noalloc(
   return fused_launch(x, x_stride, a, b, b_offsets, b_strides, y, y_stride, segment_indptr,
                       segment_slots, token_indices, ranks, scales, slice_offsets, segment_count,
                       scratch, num_tokens, width, out_width, num_slices, capacity, num_slots,
-                      max_segments, numerics, stream);
+                      max_segments, numerics, kSeg, stream);
 }

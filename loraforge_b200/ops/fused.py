@@ -62,8 +62,60 @@ def lora_shrink_expand(
     (allocated per call when omitted; pass one to keep a captured graph
     allocation-free).  A caller-owned workspace must be zero-filled before its
     first use (``torch.zeros``); every call leaves its counters at zero again, so
-    one workspace serves any sequence of calls on one stream.
+    one workspace serves any sequence of calls of the same sizes on one stream.
     """
+    _launch(
+        "lf_fused_shrink_expand", _native.fused_workspace_floats, x, a, b, output, b_offsets,
+        b_strides, ranks, scales, segment_indptr, segment_slots, token_indices, slice_offsets,
+        segment_count, num_slices, numerics, workspace,
+    )
+
+
+def prefill_workspace_floats(tokens: int, width: int, num_slices: int, capacity: int) -> int:
+    """Elements of the FP32 workspace ``lora_shrink_expand_prefill`` needs for these sizes."""
+    return _native.prefill_workspace_floats(tokens, width, num_slices, capacity)
+
+
+@ExperimentalAPI(reason="Fused BF16 prefill shrink/expand; sm_100a tcgen05 tensor cores, caller-owned metadata.")
+def lora_shrink_expand_prefill(
+    x,
+    a,
+    b,
+    output,
+    *,
+    b_offsets,
+    b_strides,
+    ranks,
+    scales,
+    segment_indptr,
+    segment_slots,
+    token_indices,
+    slice_offsets,
+    segment_count,
+    num_slices: int = 1,
+    numerics: str = "fp32",
+    workspace=None,
+) -> None:
+    """``lora_shrink_expand`` for prefill batches: segments of up to 128 tokens.
+
+    Route with ``group_tokens(..., chunk=128)``.  Segments of 16 to 128 tokens run on the
+    tcgen05 tensor cores (128-token tiles, FP32 accumulators in TMEM); shorter ones run
+    on the decode kernels in the same call.  Same operands, numerics and workspace rules
+    as ``lora_shrink_expand`` with ``prefill_workspace_floats`` for the size.  The B200
+    form of the reference's prefill SGMV (the rank-aware shrink,
+    src/loraforge/integrations/_sglang_rank_aware.py:14-171, and the chunked expand it
+    pairs with, src/loraforge/integrations/_sglang_fleet.py:310-313).
+    """
+    _launch(
+        "lf_sgmv_prefill", _native.prefill_workspace_floats, x, a, b, output, b_offsets,
+        b_strides, ranks, scales, segment_indptr, segment_slots, token_indices, slice_offsets,
+        segment_count, num_slices, numerics, workspace,
+    )
+
+
+def _launch(entry, sizer, x, a, b, output, b_offsets, b_strides, ranks, scales,
+            segment_indptr, segment_slots, token_indices, slice_offsets, segment_count,
+            num_slices, numerics, workspace):
     import torch
 
     _tensor(x, "x", 2, torch.bfloat16)
@@ -114,7 +166,7 @@ def lora_shrink_expand(
          token_indices, slice_offsets, segment_count),
     )
     capacity = a.shape[1] // num_slices
-    need = _native.fused_workspace_floats(x.shape[0], x.shape[1], num_slices, capacity)
+    need = sizer(x.shape[0], x.shape[1], num_slices, capacity)
     if workspace is None:
         workspace = torch.zeros(need, dtype=torch.float32, device=x.device)
     if (
@@ -127,13 +179,13 @@ def lora_shrink_expand(
     ):
         raise ValueError(
             f"workspace must be a contiguous 16-byte aligned FP32 buffer of >= {need} "
-            "elements on the same device (workspace_floats)"
+            f"elements on the same device ({sizer.__name__})"
         )
     if x.shape[0] == 0:
         return
     with torch.cuda.device(x.device):
         _native.call(
-            "lf_fused_shrink_expand",
+            entry,
             x.data_ptr(),
             x.stride(0),
             a.data_ptr(),
