@@ -186,11 +186,10 @@ int lf_fused_shrink_expand(const void* x, int64_t x_stride, const void* a, const
 /*
  * Grouped (SGMV) shrink -> expand for prefill batches: the arguments and numerics of
  * lf_fused_shrink_expand, with segments of up to 128 tokens (group_tokens chunk 128).
- * Segments of 16..128 tokens run on the tcgen05 tensor cores with TMEM accumulators
- * (M = 128 tokens per tile; shrink N = S*r rounded up to 16, K split in parts of 1024 whose
- * FP32 partials are added in order; expand N = 256 output columns, K = 64 zero-padded
- * rank); segments of fewer than 16 tokens run on the decode kernels of
- * lf_fused_shrink_expand in the same call.  `workspace` holds at least
+ * Every segment runs on the tcgen05 tensor cores with TMEM accumulators (M = 128 tokens
+ * per tile; shrink N = S*r rounded up to 16, K split in parts of 1024 whose FP32 partials
+ * are added in order; expand N = 256 output columns, K = 64 zero-padded rank); a short
+ * segment only leaves tile rows idle.  `workspace` holds at least
  * lf_sgmv_prefill_workspace_floats(...) floats, 16-byte aligned, zero-filled before its
  * first use (reused as for lf_fused_shrink_expand).  Replaces the prefill path of the
  * reference: the rank-aware SGMV shrink (src/loraforge/integrations/_sglang_rank_aware.py:

@@ -80,7 +80,7 @@ __global__ void __launch_bounds__(kGroupThreads)
 group_tokens_kernel(const int32_t* __restrict__ slots, int T, int num_slots, int chunk,
                     int32_t* __restrict__ indptr, int32_t* __restrict__ seg_slots,
                     int32_t* __restrict__ perm, int32_t* __restrict__ seg_count,
-                    int cache_tokens) {
+                    int cache_tokens, int blocked) {
   extern __shared__ int smem[];
   int* start = smem;                       // num_slots + 2
   int* segbase = start + num_slots + 2;    // num_slots + 1
@@ -88,6 +88,9 @@ group_tokens_kernel(const int32_t* __restrict__ slots, int T, int num_slots, int
   int* warp_b = warp_a + kGroupWarps;      // 32
   int* totals = warp_b + kGroupWarps;      // 2
   int* cache = totals + 2;                 // T when cache_tokens
+  // Blocked scatter: per-warp bucket counts [32][num_slots + 2] and per-token ranks [T].
+  uint16_t* wcount = reinterpret_cast<uint16_t*>(cache + (cache_tokens ? T : 0));
+  uint16_t* rank = wcount + kGroupWarps * (num_slots + 2);
   const int tid = threadIdx.x;
 
   for (int s = tid; s < num_slots + 2; s += kGroupThreads) start[s] = 0;
@@ -124,22 +127,58 @@ group_tokens_kernel(const int32_t* __restrict__ slots, int T, int num_slots, int
     *seg_count = nseg;
   }
   __syncthreads();
+  auto bucket_of = [&](int t) {
+    if (t >= T) return num_slots + 1;
+    if (cache_tokens) return cache[t];
+    const int sl = slots[t];
+    return (sl >= 0 && sl < num_slots) ? sl : num_slots;
+  };
+  const int lane = tid & 31, warp = tid >> 5;
+  const unsigned lower = (1u << lane) - 1u;
+  if (blocked) {
+    // Stable scatter in three parallel passes.  (1) Warp w ranks the tokens of its
+    // contiguous block in order (32 at a time, lanes of one bucket numbered by
+    // __match_any_sync) and counts them per bucket.  (2) Per bucket, the warps' counts
+    // become exclusive offsets in warp order.  (3) Every token lands at
+    // bucket start + its warp's offset + its rank inside the warp's block.
+    const int nb = num_slots + 2;
+    for (int i = tid; i < kGroupWarps * nb; i += kGroupThreads) wcount[i] = 0;
+    __syncthreads();
+    const int per = (T + kGroupWarps - 1) / kGroupWarps;
+    const int b0 = warp * per, b1 = min(T, b0 + per);
+    uint16_t* mine = wcount + warp * nb;
+    for (int base = b0; base < b1; base += 32) {
+      const int t = base + lane;
+      const int bucket = t < b1 ? bucket_of(t) : num_slots + 1;
+      const unsigned same = __match_any_sync(0xffffffffu, bucket);
+      const int r = mine[bucket] + __popc(same & lower);
+      __syncwarp();
+      if (lane == __ffs(same) - 1) mine[bucket] = uint16_t(mine[bucket] + __popc(same));
+      __syncwarp();
+      if (t < b1) rank[t] = uint16_t(r);
+    }
+    __syncthreads();
+    for (int k = tid; k < nb; k += kGroupThreads) {
+      int run = 0;
+      for (int w = 0; w < kGroupWarps; ++w) {
+        const int c = wcount[w * nb + k];
+        wcount[w * nb + k] = uint16_t(run);
+        run += c;
+      }
+    }
+    __syncthreads();
+    for (int t = tid; t < T; t += kGroupThreads) {
+      const int bucket = bucket_of(t);
+      perm[start[bucket] + wcount[(t / per) * nb + bucket] + rank[t]] = t;
+    }
+    return;
+  }
   // Stable scatter: warp 0 walks the tokens in order, 32 at a time; lanes with the
   // same bucket get consecutive positions in token order.
   if (tid < 32) {
-    const int lane = tid;
-    const unsigned lower = (1u << lane) - 1u;
     for (int base = 0; base < T; base += 32) {
       const int t = base + lane;
-      int bucket = num_slots + 1;
-      if (t < T) {
-        if (cache_tokens) {
-          bucket = cache[t];
-        } else {
-          const int s = slots[t];
-          bucket = (s >= 0 && s < num_slots) ? s : num_slots;
-        }
-      }
+      const int bucket = bucket_of(t);
       const unsigned same = __match_any_sync(0xffffffffu, bucket);
       const int pos = start[bucket] + __popc(same & lower);
       __syncwarp();
@@ -169,11 +208,16 @@ extern "C" int lf_group_tokens(const int32_t* slots, int64_t num_tokens, int32_t
   const size_t limit = 200 * 1024;
   if (fixed > limit) return fail(LF_E_INVALID, "group_tokens: too many slots");
   const int cache = fixed + sizeof(int) * size_t(T) <= limit ? 1 : 0;
-  const size_t bytes = fixed + (cache ? sizeof(int) * size_t(T) : 0);
+  size_t bytes = fixed + (cache ? sizeof(int) * size_t(T) : 0);
+  // The parallel blocked scatter needs 16-bit per-warp counts and ranks in shared memory.
+  const size_t blocked_extra =
+      sizeof(uint16_t) * (size_t(kGroupWarps) * (num_slots + 2) + size_t(T) + 1);
+  const int blocked = T >= 64 && T <= 65535 && bytes + blocked_extra + 16 <= limit ? 1 : 0;
+  if (blocked) bytes += blocked_extra + 16;
   static int flags[64] = {};
   if (int rc = ensure_smem(group_tokens_kernel, int(limit), flags)) return rc;
   group_tokens_kernel<<<1, kGroupThreads, bytes, static_cast<cudaStream_t>(stream)>>>(
       slots, T, num_slots, chunk, segment_indptr, segment_slots, token_indices,
-      segment_count, cache);
+      segment_count, cache, blocked);
   return check_launch("group_tokens");
 }

@@ -21,9 +21,8 @@ int64_t decode_scratch_floats(int64_t num_tokens, int64_t width, int num_slices,
 Scratch decode_scratch(float* region, int64_t num_tokens, int64_t width, int num_slices,
                        int capacity);
 
-// The decode shrink -> expand pair over the segments of at most `max_tokens` tokens
-// (16 for lf_fused_shrink_expand; 15 when the prefill entry point leaves them the
-// segments below its 16-token tcgen05 threshold).  Arguments as lf_fused_shrink_expand.
+// The decode shrink -> expand pair over the segments of at most `max_tokens` (<= 16)
+// tokens; longer segments are skipped.  Arguments as lf_fused_shrink_expand.
 int fused_launch(const void* x, int64_t x_stride, const void* a, const void* b,
                  const int64_t* b_offsets, const int32_t* b_strides, void* y, int64_t y_stride,
                  const int32_t* segment_indptr, const int32_t* segment_slots,

@@ -19,14 +19,21 @@
 //                          TMEM accumulators; eight epilogue warps read the other one and
 //                          update the y rows (prefetched before the MMA completes).
 //
-// Segments with fewer than 16 tokens are left to the decode kernels (sgmv.cu), which the
-// entry point launches after these two.  Numerics follow lf_fused_shrink_expand: FP32
+// Every segment of a prefill call runs on these tiles, short ones included: a tile's unused
+// rows cost tensor-core cycles but no memory traffic (x and y rows are moved only for the
+// segment's tokens, A and B once per tile either way), while sending the short segments
+// to the decode kernels costs two more launches (measured on BASELINE config 3: 57 us for
+// two segments of under 16 tokens, against 0 extra here).  Numerics follow lf_fused_shrink_expand: FP32
 // keeps z in FP32 (hi + lo BF16 parts) and rounds y once; "reference" rounds z to BF16
 // and the scaled delta to BF16 before the BF16 sum (src/loraforge/ops/csrc/lora_rows.cu:64
 // and :113).
 //
 // Every wait is bounded (tma.cuh): an expired wait is counted and the thread carries on
 // to the CTA's final barrier, where the TMEM allocation is always released.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
 #include <string>
 
 #include "launch.cuh"
@@ -39,7 +46,7 @@ namespace {
 constexpr int kTileM = 128;                  // tokens per tile (UMMA M)
 constexpr int kRowBytes = 128;               // one swizzled K-major row: 64 BF16
 constexpr int kXTileBytes = kTileM * kRowBytes;  // 16 KiB
-constexpr int kMinTokens = 16;               // shorter segments: decode kernels
+constexpr int kMaxTokens = 128;              // tokens per segment (one tile)
 constexpr int kMaxSlices = 4;
 constexpr int kMaxRank = 64;
 constexpr int kShrinkStages = 4;
@@ -48,6 +55,7 @@ constexpr int kNT = 256;                     // expand columns per unit (UMMA N)
 constexpr int kBTileBytes = kNT * kRowBytes; // 32 KiB
 constexpr int kExpandThreads = 352;          // 8 epilogue, 2 producer, 1 MMA warp
 constexpr int kPartLen = 1024;               // K elements per shrink part
+constexpr int kBStages = 3;                  // expand B-tile ring
 
 enum Numerics { kFp32 = 0, kReference = 1 };
 
@@ -67,12 +75,16 @@ struct PParams {
   const float* scales;
   const int32_t* slice_offsets;
   const int32_t* seg_count;
-  float* partial;  // [kparts][T][rpad]
-  float* zfinal;   // [T][rpad]
-  int* counters;   // [T], zero between calls
+  float* partial;     // [kparts][T][rpad]
+  float* zfinal;      // [T][rpad]: z of each token (row = permuted position)
+  int* counters;      // [T], zero between calls
   int T, K, N, S, cap, num_slots, max_segments;
-  int rpad;    // shrink UMMA N: S*min(cap, 64) rounded up to 16 (<= 256)
-  int kparts;  // K parts of kPartLen
+  int rpad;      // shrink UMMA N: S*min(cap, 64) rounded up to 16 (<= 256)
+  int kparts;    // K parts of kPartLen
+  int numerics;  // kFp32 or kReference
+  int pad;
+  CUtensorMap tmap_x;  // x as 2-D [T rows, K], boxes of 128 rows x 64 columns, 128-B swizzle
+  CUtensorMap tmap_a;  // A as 2-D [slots*S*cap rows, K], boxes of rpad rows x 64 columns
 };
 
 struct PSeg {
@@ -91,15 +103,15 @@ __device__ __forceinline__ int segment_total(const PParams& p) {
   return max(0, min(n, min(p.max_segments, p.T)));
 }
 
-// Segment metadata; ok only for segments of kMinTokens..kTileM tokens whose slot, rank,
-// bucket and B offset are inside the contract (others are skipped by every role).
+// Segment metadata; ok only for segments of 1..128 tokens whose slot, rank, bucket and
+// B offset are inside the contract (others are skipped by every role).
 __device__ __forceinline__ PSeg prefill_segment(const PParams& p, int seg) {
   PSeg s{};
   const int lo = p.indptr[seg], hi = p.indptr[seg + 1];
   s.pos0 = lo;
   s.n = hi - lo;
   s.g = p.seg_slots[seg];
-  bool ok = lo >= 0 && hi <= p.T && s.n >= kMinTokens && s.n <= kTileM && s.g >= 0 &&
+  bool ok = lo >= 0 && hi <= p.T && s.n >= 1 && s.n <= kMaxTokens && s.g >= 0 &&
             s.g < p.num_slots;
   if (ok) {
     s.r = p.ranks[s.g];
@@ -224,16 +236,39 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return (float_to_bf16_bits(lo) & 0xffffu) | (float_to_bf16_bits(hi) << 16);
 }
 
+// Round-to-nearest-even FP32 pair -> packed BF16 pair in one hardware conversion
+// (`first` in the low half); identical to pack_bf16 for finite values.
+__device__ __forceinline__ uint32_t cvt_bf16x2(float first, float second) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(second), "f"(first));
+  return r;
+}
+
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return p + ((1024u - (smem_u32(p) & 1023u)) & 1023u);
 }
 
 // ====================================================================== shrink
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, "
+      "{%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Stage: x tile (128 rows) then A tile (rpad rows), both K-major with 128-byte rows and
+// 128-byte swizzle.  A arrives as one 2-D TMA box; x too when the chunk's tokens are one
+// contiguous run of rows (the usual prefill case), else each producer thread gathers its
+// row with cp.async.  The stage's "full" barrier takes 129 arrivals: thread 0's
+// expect-tx arrive for the TMA bytes and one arrive per producer thread once its own
+// copies (if any) have landed and been made visible to the tensor cores' proxy.
 __global__ void __launch_bounds__(kShrinkThreads, 1) prefill_shrink_kernel(const __grid_constant__ PParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int SB = kXTileBytes + p.rpad * kRowBytes;  // stage: x tile, then A tile
+  const int SB = kXTileBytes + p.rpad * kRowBytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kShrinkStages * SB);
   uint64_t* empty = full + kShrinkStages;
   uint64_t* acc_full = empty + kShrinkStages;
@@ -246,7 +281,7 @@ __global__ void __launch_bounds__(kShrinkThreads, 1) prefill_shrink_kernel(const
 
   if (tid == 0) {
     for (int s = 0; s < kShrinkStages; ++s) {
-      mbar_init(&full[s], kTileM);
+      mbar_init(&full[s], kTileM + 1);
       mbar_init(&empty[s], 1);
     }
     mbar_init(acc_full, 1);
@@ -277,14 +312,16 @@ __global__ void __launch_bounds__(kShrinkThreads, 1) prefill_shrink_kernel(const
       const int k0 = kp * kPartLen;
       const int kend = min(p.K, k0 + kPartLen);
       const int nsteps = (kend - k0 + 63) / 64;
-      const int R = p.S * si.r;
       int tok = -1;
       if (row < si.n) {
         tok = p.perm[si.pos0 + row];
         if (tok < 0 || tok >= p.T) tok = -1;
       }
+      // token_indices is ascending inside a slot's group: equal spans mean one run.
+      const int first = p.perm[si.pos0], last = p.perm[si.pos0 + si.n - 1];
+      const bool run = first >= 0 && last < p.T && last - first == si.n - 1;
       const uint16_t* xrow = tok >= 0 ? p.x + int64_t(tok) * p.x_stride : p.x;
-      const uint16_t* arows = p.a + int64_t(si.g) * p.S * p.cap * p.K;
+      const int arow0 = si.g * p.S * p.cap;
       int pend0 = -1, pend1 = -1;
       for (int s = 0; s < nsteps; ++s, ++sidx) {
         const int stage = sidx % kShrinkStages;
@@ -292,21 +329,24 @@ __global__ void __launch_bounds__(kShrinkThreads, 1) prefill_shrink_kernel(const
         wait_or_abort(&empty[stage], phase ^ 1u, abort);
         const uint32_t st = smem_u32(smem + stage * SB);
         const int kk = k0 + s * 64;
+        if (tid == 0) {
+          mbar_arrive_expect_tx(&full[stage], uint32_t(p.rpad * kRowBytes + (run ? kXTileBytes : 0)));
+          tma_load_2d(st + kXTileBytes, &p.tmap_a, kk, arow0, &full[stage]);
+          if (run) tma_load_2d(st, &p.tmap_x, kk, first, &full[stage]);
+        }
+        if (run) {
+          mbar_arrive(&full[stage]);
+          continue;
+        }
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           const int kc = kk + 8 * c;
           const bool v = tok >= 0 && kc < kend;
           cp16(st + swz(row, c), v ? static_cast<const void*>(xrow + kc) : p.x, v ? 16u : 0u);
         }
-        for (int i = tid; i < p.rpad * 8; i += kTileM) {
-          const int j = i >> 3, c = i & 7, kc = kk + 8 * c;
-          const bool v = j < R && kc < kend;
-          cp16(st + kXTileBytes + swz(j, c), v ? static_cast<const void*>(arows + int64_t(j) * p.K + kc) : p.a,
-               v ? 16u : 0u);
-        }
         cp_commit();
-        // Hand a stage to the MMA thread two steps later: its copies are complete and
-        // made visible to the tensor cores' (async) proxy.
+        // Arrive for a gathered stage two steps later, once its copies have landed and
+        // are visible to the tensor cores' (async) proxy.
         if (pend1 >= 0) {
           cp_wait<2>();
           fence_async_smem();
@@ -319,10 +359,12 @@ __global__ void __launch_bounds__(kShrinkThreads, 1) prefill_shrink_kernel(const
           pend0 = stage;
         }
       }
-      cp_wait<0>();
-      fence_async_smem();
-      if (pend0 >= 0) mbar_arrive(&full[pend0]);
-      if (pend1 >= 0) mbar_arrive(&full[pend1]);
+      if (!run) {
+        cp_wait<0>();
+        fence_async_smem();
+        if (pend0 >= 0) mbar_arrive(&full[pend0]);
+        if (pend1 >= 0) mbar_arrive(&full[pend1]);
+      }
 
       // Epilogue: accumulator rows -> this K part's partial.
       wait_or_abort(acc_full, uint32_t(units) & 1u, abort);
@@ -343,7 +385,7 @@ __global__ void __launch_bounds__(kShrinkThreads, 1) prefill_shrink_kernel(const
       }
       tc_fence_before();
       mbar_arrive(acc_empty);
-      // The CTA that completes the segment's count adds the parts in order.
+      // The CTA that completes the segment's count adds the parts in order into z.
       __threadfence();
       named_barrier(1, kTileM);
       if (tid == 0) {
@@ -355,16 +397,28 @@ __global__ void __launch_bounds__(kShrinkThreads, 1) prefill_shrink_kernel(const
         __threadfence();
         if (row < si.n) {
           const int64_t pos = si.pos0 + row;
-          for (int j = 0; j < p.rpad; j += 4) {
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int jb = 0; jb < p.rpad; jb += 64) {
+            const int nv = min(64, p.rpad - jb) / 4;  // float4s in this block (rpad % 16 == 0)
+            float4 acc[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
             for (int q = 0; q < p.kparts; ++q) {
-              const float4 v = __ldcg(reinterpret_cast<const float4*>(p.partial + (int64_t(q) * p.T + pos) * p.rpad + j));
-              acc.x += v.x;
-              acc.y += v.y;
-              acc.z += v.z;
-              acc.w += v.w;
+              const float4* src = reinterpret_cast<const float4*>(p.partial + (int64_t(q) * p.T + pos) * p.rpad + jb);
+              float4 v[16];
+#pragma unroll
+              for (int i = 0; i < 16; ++i) v[i] = i < nv ? __ldcg(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                acc[i].x += v[i].x;
+                acc[i].y += v[i].y;
+                acc[i].z += v[i].z;
+                acc[i].w += v[i].w;
+              }
             }
-            *reinterpret_cast<float4*>(p.zfinal + pos * p.rpad + j) = acc;
+            float4* dst = reinterpret_cast<float4*>(p.zfinal + pos * p.rpad + jb);
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (i < nv) dst[i] = acc[i];
           }
         }
         if (tid == 0) p.counters[seg] = 0;
@@ -379,9 +433,9 @@ __global__ void __launch_bounds__(kShrinkThreads, 1) prefill_shrink_kernel(const
       const int seg = u / p.kparts, kp = u - seg * p.kparts;
       const PSeg si = prefill_segment(p, seg);
       if (!si.ok) continue;
+      if (*abort) break;
       const int k0 = kp * kPartLen;
       const int nsteps = (min(p.K, k0 + kPartLen) - k0 + 63) / 64;
-      if (*abort) break;
       if (units > 0) wait_or_abort(acc_empty, uint32_t(units - 1) & 1u, abort);
       tc_fence_after();
       for (int s = 0; s < nsteps; ++s, ++sidx) {
@@ -438,11 +492,11 @@ __global__ void __launch_bounds__(kExpandThreads, 1) prefill_expand_kernel(const
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  uint8_t* btile = smem;                   // 2 x 32 KiB
-  uint8_t* ztile = smem + 2 * kBTileBytes;  // 2 buffers x (hi, lo) x 16 KiB
+  uint8_t* btile = smem;                           // kBStages x 32 KiB
+  uint8_t* ztile = smem + kBStages * kBTileBytes;  // 2 buffers x (hi, lo) x 16 KiB
   uint64_t* b_full = reinterpret_cast<uint64_t*>(ztile + 4 * kXTileBytes);
-  uint64_t* b_empty = b_full + 2;
-  uint64_t* z_full = b_empty + 2;
+  uint64_t* b_empty = b_full + kBStages;
+  uint64_t* z_full = b_empty + kBStages;
   uint64_t* z_empty = z_full + 2;
   uint64_t* t_full = z_empty + 2;
   uint64_t* t_empty = t_full + 2;
@@ -453,9 +507,11 @@ __global__ void __launch_bounds__(kExpandThreads, 1) prefill_expand_kernel(const
   constexpr int kEpi = 256, kProd = 64;
 
   if (tid == 0) {
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kBStages; ++i) {
       mbar_init(&b_full[i], kProd);
       mbar_init(&b_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&z_full[i], kProd);
       mbar_init(&z_empty[i], 1);
       mbar_init(&t_full[i], 1);
@@ -484,16 +540,16 @@ __global__ void __launch_bounds__(kExpandThreads, 1) prefill_expand_kernel(const
     // ------------------------------------------------------------ producers
     const int pt = tid - kEpi;
     bool waited = false;
-    int bidx = 0, zcount = 0, key = -1;
+    int bidx = 0, zcount = 0, key = -1, pend = -1;
     for (int u = u0; u < u1; ++u) {
       const int seg = u / nb;
       const Block blk = block_of(offs, p.S, u - seg * nb);
       const PSeg si = prefill_segment(p, seg);
       if (!si.ok || blk.slice < 0) continue;
-      // B rows of the block, zero-padded to 64 elements.
       if (*abort) break;
-      const int bs = bidx & 1;
-      wait_or_abort(&b_empty[bs], (uint32_t(bidx >> 1) & 1u) ^ 1u, abort);
+      // B rows of the block, zero-padded to 64 elements (3-stage ring).
+      const int bs = bidx % kBStages;
+      wait_or_abort(&b_empty[bs], (uint32_t(bidx / kBStages) & 1u) ^ 1u, abort);
       ++bidx;
       const uint32_t bt = smem_u32(btile + bs * kBTileBytes);
       const int gcol0 = offs[blk.slice] + blk.c0;
@@ -501,8 +557,8 @@ __global__ void __launch_bounds__(kExpandThreads, 1) prefill_expand_kernel(const
         const int r = i >> 3, c = i & 7, k = 8 * c;
         const bool live = blk.c0 + r < blk.width && k < si.bucket;
         const uint16_t* src = p.b + si.boff + int64_t(gcol0 + r) * si.bucket + k;
-        if (live && si.bucket >= 8) {
-          cp16(bt + swz(r, c), src, 16u);
+        if (si.bucket >= 8) {
+          cp16(bt + swz(r, c), live ? static_cast<const void*>(src) : p.b, live ? 16u : 0u);
         } else {
           uint32_t w[4] = {0u, 0u, 0u, 0u};
           if (live)
@@ -511,46 +567,78 @@ __global__ void __launch_bounds__(kExpandThreads, 1) prefill_expand_kernel(const
         }
       }
       cp_commit();
-      cp_wait<0>();
-      fence_async_smem();
-      mbar_arrive(&b_full[bs]);
-      // z tile of (segment, slice), rebuilt when it changes.
+      // The previous block is handed over once its copies have landed (one block of
+      // lag keeps two in flight).
+      if (pend >= 0) {
+        cp_wait<1>();
+        fence_async_smem();
+        mbar_arrive(&b_full[pend]);
+      }
+      pend = bs;
+      // z tile of (segment, slice): the shrink's BF16 hi / lo rows, swizzled.
       const int k2 = seg * kMaxSlices + blk.slice;
       if (k2 != key) {
         key = k2;
         if (!waited) {
-          pdl_wait();  // z is written by the preceding shrink grid
+          pdl_wait();  // the z rows are written by the preceding shrink grid
           waited = true;
         }
         const int zb = zcount & 1;
         wait_or_abort(&z_empty[zb], (uint32_t(zcount >> 1) & 1u) ^ 1u, abort);
         ++zcount;
+        // BF16 hi + lo of scale * z (FP32 numerics) or bf16(z) (reference), zero beyond
+        // min(rank, bucket) and past the segment's rows; 8 elements per thread step.
         const uint32_t zh = smem_u32(ztile + zb * 2 * kXTileBytes), zl = zh + kXTileBytes;
         const int live = min(si.r, si.bucket);
         const float mul = MODE == kFp32 ? si.scale : 1.f;
-        for (int i = pt; i < kTileM * 8; i += kProd) {
-          const int m = i >> 3, c = i & 7;
-          float v[8];
+        const int col0 = blk.slice * si.r;
+        const bool vec = (col0 & 3) == 0;
+        // Four items per pass: all their loads are issued before any conversion.
+        for (int i0 = pt; i0 < kTileM * 8; i0 += 4 * kProd) {
+          float v[4][8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const int k = 8 * c + e;
-            v[e] = (m < si.n && k < live)
-                       ? mul * __ldcg(p.zfinal + int64_t(si.pos0 + m) * p.rpad + blk.slice * si.r + k)
-                       : 0.f;
-          }
-          uint32_t hw[4], lw[4];
+          for (int q = 0; q < 4; ++q) {
+            const int i = i0 + q * kProd, m = i >> 3, c = i & 7;
+            const float* src = p.zfinal + int64_t(si.pos0 + m) * p.rpad + col0 + 8 * c;
+            if (i < kTileM * 8 && m < si.n && vec && 8 * c + 8 <= live) {
+              const float4 a0 = __ldcg(reinterpret_cast<const float4*>(src));
+              const float4 a1 = __ldcg(reinterpret_cast<const float4*>(src) + 1);
+              v[q][0] = a0.x; v[q][1] = a0.y; v[q][2] = a0.z; v[q][3] = a0.w;
+              v[q][4] = a1.x; v[q][5] = a1.y; v[q][6] = a1.z; v[q][7] = a1.w;
+            } else {
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float h0 = round_through_bf16(v[2 * e]), h1 = round_through_bf16(v[2 * e + 1]);
-            hw[e] = pack_bf16(h0, h1);
-            lw[e] = pack_bf16(v[2 * e] - h0, v[2 * e + 1] - h1);
+              for (int e = 0; e < 8; ++e)
+                v[q][e] = (i < kTileM * 8 && m < si.n && 8 * c + e < live) ? __ldcg(src + e) : 0.f;
+            }
           }
-          sts16(zh + swz(m, c), make_uint4(hw[0], hw[1], hw[2], hw[3]));
-          if (MODE == kFp32) sts16(zl + swz(m, c), make_uint4(lw[0], lw[1], lw[2], lw[3]));
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int i = i0 + q * kProd, m = i >> 3, c = i & 7;
+            if (i >= kTileM * 8) break;
+            uint32_t hw[4], lw[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float v0 = mul * v[q][2 * e], v1 = mul * v[q][2 * e + 1];
+              hw[e] = cvt_bf16x2(v0, v1);
+              const float h0 = __uint_as_float(hw[e] << 16), h1 = __uint_as_float(hw[e] & 0xffff0000u);
+              lw[e] = cvt_bf16x2(v0 - h0, v1 - h1);
+            }
+            sts16(zh + swz(m, c), make_uint4(hw[0], hw[1], hw[2], hw[3]));
+            if (MODE == kFp32) sts16(zl + swz(m, c), make_uint4(lw[0], lw[1], lw[2], lw[3]));
+          }
         }
+        cp_commit();
+        cp_wait<0>();
         fence_async_smem();
+        mbar_arrive(&b_full[pend]);
+        pend = -1;
         mbar_arrive(&z_full[zb]);
       }
+    }
+    if (pend >= 0) {
+      cp_wait<0>();
+      fence_async_smem();
+      mbar_arrive(&b_full[pend]);
     }
     // Every CTA waits for the shrink grid, so this grid's completion implies the shrink's.
     if (!waited) pdl_wait();
@@ -573,8 +661,8 @@ __global__ void __launch_bounds__(kExpandThreads, 1) prefill_expand_kernel(const
           wait_or_abort(&z_full[zb], uint32_t(zcount >> 1) & 1u, abort);
           ++zcount;
         }
-        const int bs = bidx & 1;
-        wait_or_abort(&b_full[bs], uint32_t(bidx >> 1) & 1u, abort);
+        const int bs = bidx % kBStages;
+        wait_or_abort(&b_full[bs], uint32_t(bidx / kBStages) & 1u, abort);
         ++bidx;
         const int tb = tcount & 1;
         wait_or_abort(&t_empty[tb], (uint32_t(tcount >> 1) & 1u) ^ 1u, abort);
@@ -647,7 +735,7 @@ __global__ void __launch_bounds__(kExpandThreads, 1) prefill_expand_kernel(const
               const float y0 = __uint_as_float(ow[e] << 16), y1 = __uint_as_float(ow[e] & 0xffff0000u);
               const float v0 = MODE == kFp32 ? y0 + d0 : y0 + round_through_bf16(d0 * si.scale);
               const float v1 = MODE == kFp32 ? y1 + d1 : y1 + round_through_bf16(d1 * si.scale);
-              nw[e] = pack_bf16(v0, v1);
+              nw[e] = cvt_bf16x2(v0, v1);
             }
             *reinterpret_cast<uint4*>(yrow + 32 * ch + 8 * i) = make_uint4(nw[0], nw[1], nw[2], nw[3]);
           }
@@ -677,7 +765,7 @@ __global__ void __launch_bounds__(kExpandThreads, 1) prefill_expand_kernel(const
 // ====================================================================== host side
 struct PrefillLayout {
   int rpad, kparts;
-  int64_t partial, zfinal, counters, decode, total;  // offsets in floats
+  int64_t partial, zfinal, counters, total;  // offsets in floats
 };
 
 inline PrefillLayout prefill_layout(int64_t tokens, int64_t width, int num_slices, int capacity) {
@@ -689,9 +777,24 @@ inline PrefillLayout prefill_layout(int64_t tokens, int64_t width, int num_slice
   l.partial = 0;
   l.zfinal = l.partial + int64_t(l.kparts) * T * l.rpad;
   l.counters = l.zfinal + T * l.rpad;
-  l.decode = l.counters + (T + 3) / 4 * 4;
-  l.total = l.decode + decode_scratch_floats(tokens, width, num_slices, capacity);
+  l.total = l.counters + (T + 3) / 4 * 4;
   return l;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
+inline PFN_cuTensorMapEncodeTiled_v12000 prefill_tensor_map_encoder() {
+  static std::mutex mutex;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::lock_guard<std::mutex> lock(mutex);
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult status;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &status) ==
+            cudaSuccess &&
+        status == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
 }
 
 template <typename Kernel>
@@ -779,32 +882,46 @@ extern "C" int lf_sgmv_prefill(
             y_stride, segment_indptr, segment_slots, token_indices, ranks, scales, slice_offsets,
             segment_count, workspace + l.partial, workspace + l.zfinal,
             reinterpret_cast<int*>(workspace + l.counters), int(T), int(width), out_width,
-            num_slices, capacity, num_slots, max_segments, l.rpad, l.kparts};
+            num_slices, capacity, num_slots, max_segments, l.rpad, l.kparts, numerics, 0};
+  {
+    // x [T, K] and A [slots*S*cap, K] as 2-D tensors for the shrink's TMA boxes.
+    const PFN_cuTensorMapEncodeTiled_v12000 encode = prefill_tensor_map_encoder();
+    if (!encode) return fail(LF_E_CUDA, "sgmv_prefill: cuTensorMapEncodeTiled unavailable");
+    const cuuint32_t estr[2] = {1, 1};
+    const cuuint64_t xdims[2] = {cuuint64_t(width), cuuint64_t(T)};
+    const cuuint64_t xstrides[1] = {cuuint64_t(x_stride) * 2};
+    const cuuint32_t xbox[2] = {64, kTileM};
+    const cuuint64_t adims[2] = {cuuint64_t(width), cuuint64_t(num_slots) * num_slices * capacity};
+    const cuuint64_t astrides[1] = {cuuint64_t(width) * 2};
+    const cuuint32_t abox[2] = {64, cuuint32_t(l.rpad)};
+    CUresult r = encode(&p.tmap_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), xdims,
+                        xstrides, xbox, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r == CUDA_SUCCESS)
+      r = encode(&p.tmap_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(a), adims, astrides,
+                 abox, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(LF_E_CUDA, "sgmv_prefill: cuTensorMapEncodeTiled failed");
+  }
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // Long segments on the tensor cores: shrink (2 CTAs per SM), then expand (1 per SM).
+  // Shrink (2 CTAs per SM), then expand (1 per SM), all segments on the tensor cores.
   {
     const int smem = kShrinkStages * (kXTileBytes + l.rpad * kRowBytes) + 1024 + 128;
     static int flags[64] = {};
     if (int rc = ensure_smem(prefill_shrink_kernel, smem, flags)) return rc;
-    const int64_t long_cap = T / kMinTokens < seg_cap ? T / kMinTokens + 1 : seg_cap;
-    const int64_t units = long_cap * l.kparts;
+    const int64_t units = seg_cap * l.kparts;
     const int grid = int(units < 2 * sms ? units : 2 * sms);
     if (int rc = launch_pdl(prefill_shrink_kernel, grid, kShrinkThreads, smem, s, p,
                             "sgmv_prefill (shrink)"))
       return rc;
   }
   {
-    const int smem = 2 * kBTileBytes + 4 * kXTileBytes + 1024 + 256;
+    const int smem = kBStages * kBTileBytes + 4 * kXTileBytes + 1024 + 256;
     auto kernel = numerics == kFp32 ? prefill_expand_kernel<kFp32> : prefill_expand_kernel<kReference>;
     static int flags[2][64] = {};
     if (int rc = ensure_smem(kernel, smem, flags[numerics])) return rc;
     const int grid = sms;
     if (int rc = launch_pdl(kernel, grid, kExpandThreads, smem, s, p, "sgmv_prefill (expand)")) return rc;
   }
-  // Short segments (fewer than 16 tokens) on the decode kernels, in their own region.
-  const Scratch dec = decode_scratch(workspace + l.decode, num_tokens, width, num_slices, capacity);
-  return fused_launch(x, x_stride, a, b, b_offsets, b_strides, y, y_stride, segment_indptr,
-                      segment_slots, token_indices, ranks, scales, slice_offsets, segment_count,
-                      dec, num_tokens, width, out_width, num_slices, capacity, num_slots,
-                      max_segments, numerics, kMinTokens - 1, stream);
+  return LF_OK;
 }

@@ -98,9 +98,9 @@ def lora_shrink_expand_prefill(
 ) -> None:
     """``lora_shrink_expand`` for prefill batches: segments of up to 128 tokens.
 
-    Route with ``group_tokens(..., chunk=128)``.  Segments of 16 to 128 tokens run on the
-    tcgen05 tensor cores (128-token tiles, FP32 accumulators in TMEM); shorter ones run
-    on the decode kernels in the same call.  Same operands, numerics and workspace rules
+    Route with ``group_tokens(..., chunk=128)``.  Every segment runs on the tcgen05 tensor
+    cores (128-token tiles, FP32 accumulators in TMEM; a short segment leaves tile rows
+    idle but moves no extra x or y bytes).  Same operands, numerics and workspace rules
     as ``lora_shrink_expand`` with ``prefill_workspace_floats`` for the size.  The B200
     form of the reference's prefill SGMV (the rank-aware shrink,
     src/loraforge/integrations/_sglang_rank_aware.py:14-171, and the chunked expand it
