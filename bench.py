@@ -105,7 +105,26 @@ CONFIGS = {
         "64 adapters r=64, 5120->5120",
         tokens=8192, slots=64, cap=64, projections=(("proj", 5120, (5120,)),), prefill=True,
     ),
+    4: dict(
+        workload="config4: tensor-parallel decode, hidden 5120, intermediate 27648, 512 tokens, "
+        "1024 adapters r=32, Zipf(1.0); gate/up column-parallel, down row-parallel with an "
+        "all-reduce of the FP32 z rows",
+        tokens=512, slots=1024, cap=32, hidden=5120, inter=27648, sharded=True,
+    ),
 }
+
+
+def config_projections(config, world):
+    """(name, in_dim, slice widths) of each projection on one rank of `world`."""
+    c = CONFIGS[config]
+    if not c.get("sharded"):
+        return c["projections"]
+    h, f = c["hidden"], c["inter"]
+    if f % world or h % world:
+        raise SystemExit(f"config {config} needs a rank count dividing {f} and {h}")
+    # gate/up: full input, this rank's columns of both slices; down: this rank's input
+    # columns and output columns.
+    return (("gate_up_proj", h, (f // world, f // world)), ("down_proj", f // world, (h // world,)))
 
 
 def config_routing(config, rng):
@@ -116,6 +135,10 @@ def config_routing(config, rng):
         ranks = np.full(G, 16)
         scales = np.full(G, 2.0)
         slots = zipf_slots(rng, T, G, 1.1)
+    elif config == 4:
+        ranks = np.full(G, 32)
+        scales = np.full(G, 2.0)
+        slots = zipf_slots(rng, T, G, 1.0)
     elif config == 2:
         ranks = rng.choice([4, 8, 16, 32, 64], size=G)
         scales = 16.0 / np.sqrt(ranks)
@@ -178,7 +201,7 @@ class Projection:
 
 
 class Workload:
-    def __init__(self, config, device, seed):
+    def __init__(self, config, device, seed, world=1):
         import torch
 
         from loraforge_b200.ops.grouping import empty_routing
@@ -188,16 +211,18 @@ class Workload:
         rng = np.random.default_rng(seed)
         self.config, self.device, self.T, self.nslots = config, device, c["tokens"], c["slots"]
         self.prefill = c.get("prefill", False)
+        self.sharded, self.world = c.get("sharded", False), world
+        projections = config_projections(config, world)
         self.ranks_np, self.scales_np, self.slots_np = config_routing(config, rng)
         self.slots = torch.from_numpy(self.slots_np).to(device)
         self.x = {}
-        for _, k, _ in c["projections"]:
+        for _, k, _ in projections:
             if k not in self.x:
                 self.x[k] = torch.randn(self.T, k, generator=gen, device=device).bfloat16()
         self.projections = [
             Projection(n, k, w, self.ranks_np, self.scales_np, c["cap"], self.T, device, gen,
                        c.get("prefill", False))
-            for n, k, w in c["projections"]
+            for n, k, w in projections
         ]
         self.routing = empty_routing(self.T, device)
         self.touched = np.unique(self.slots_np[self.slots_np >= 0])
@@ -216,19 +241,27 @@ class Workload:
         return sum(p.flops(self.slots_np) for p in self.projections)
 
 
-def run_step(w, events=None):
+def run_step(w, mark=None):
     """Grouping + LoRA shrink/expand of every projection through the public API.
 
     ``w.path == "fused"``: lora_shrink_expand per projection (prefill configs:
-    lora_shrink_expand_prefill over segments of up to 128 tokens, tcgen05 tiles for the
-    segments of 16 or more); ``"rows"``: row_shrink + row_expand per projection (the
-    reference's operator pair).  ``events[i]`` = (start, mid, end) CUDA events around
-    projection i's launches.
+    lora_shrink_expand_prefill over segments of up to 128 tokens on the tcgen05 tiles);
+    ``"rows"``: row_shrink + row_expand per projection (the reference's operator pair);
+    tensor-parallel configs: gate/up column-parallel, down as shrink, all-reduce of the
+    z rows over the ranks, expand.  ``mark(label)``, when given, records a CUDA event
+    that starts the interval named `label` (ended by the next mark or "end").
     """
     from loraforge_b200.ops import row_expand, row_shrink
-    from loraforge_b200.ops.fused import lora_shrink_expand, lora_shrink_expand_prefill
+    from loraforge_b200.ops.fused import (
+        lora_shrink_expand,
+        lora_shrink_expand_prefill,
+        sgmv_expand,
+        sgmv_shrink,
+        z_rows,
+    )
     from loraforge_b200.ops.grouping import group_tokens
 
+    mark = mark or (lambda label: None)
     prefill = w.prefill and w.path == "fused"
     fused_op = lora_shrink_expand_prefill if prefill else lora_shrink_expand
     r = group_tokens(w.slots, w.nslots, chunk=128 if prefill else 16, out=w.routing)
@@ -236,26 +269,34 @@ def run_step(w, events=None):
         segment_indptr=r.segment_indptr, segment_slots=r.segment_slots,
         token_indices=r.token_indices, segment_count=r.segment_count,
     )
-    for i, p in enumerate(w.projections):
+    for p in w.projections:
         meta = dict(b_offsets=p.b_offsets, b_strides=p.b_strides, ranks=p.ranks,
                     scales=p.scales, slice_offsets=p.slice_offsets, **routing)
-        if events is not None:
-            events[i][0].record()
-        if w.path == "fused":
-            fused_op(w.x_of(p), p.a, p.b, p.y, **meta, num_slices=p.S, workspace=p.workspace)
-            if events is not None:
-                events[i][1].record()
+        x = w.x_of(p)
+        if w.sharded and p.name == "down_proj":
+            mark(f"{p.name}.shrink")
+            sgmv_shrink(x, p.a, p.b, p.y, workspace=p.workspace, **meta, num_slices=p.S)
+            if w.world > 1:
+                import torch.distributed as dist
+
+                mark(f"{p.name}.allreduce")
+                dist.all_reduce(z_rows(p.workspace, w.T, p.K, p.S, p.cap))
+            mark(f"{p.name}.expand")
+            sgmv_expand(x, p.a, p.b, p.y, workspace=p.workspace, **meta, num_slices=p.S)
+        elif w.path == "fused":
+            mark(f"{p.name}.fused")
+            fused_op(x, p.a, p.b, p.y, **meta, num_slices=p.S, workspace=p.workspace)
         else:
-            row_shrink(w.x_of(p), p.a, p.z, w.slots, p.ranks, num_slices=p.S, max_rank=p.cap)
-            if events is not None:
-                events[i][1].record()
+            mark(f"{p.name}.shrink")
+            row_shrink(x, p.a, p.z, w.slots, p.ranks, num_slices=p.S, max_rank=p.cap)
+            mark(f"{p.name}.expand")
             row_expand(p.z, p.b, p.y, **meta)
-        if events is not None:
-            events[i][2].record()
+    mark("end")
 
 
 def launches_per_step(w):
-    return 1 + 2 * len(w.projections)  # grouping + two kernels per projection
+    # grouping + two kernels per projection (shrink and expand; the prefill pair too)
+    return 1 + 2 * len(w.projections)
 
 
 # ----------------------------------------------------------------------------- clocks
@@ -366,20 +407,21 @@ def time_graph(w, steps, warmup, flush):
     del graph
     # Kernel breakdown: eager launches queued behind a device sleep so that host
     # launch latency never shows up between the events; L2 flushed before each step.
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in w.projections]
-    kinds = ("fused",) if w.path == "fused" else ("shrink", "expand")
-    per_kernel = {f"{p.name}.{k}": [] for p in w.projections for k in kinds}
+    per_kernel = {}
     for _ in range(min(steps, 50)):
+        marks = []
+
+        def mark(label):
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            marks.append((label, e))
+
         flush.zero_()
         torch.cuda._sleep(4_000_000)
-        run_step(w, events=ev)
+        run_step(w, mark=mark)
         torch.cuda.synchronize()
-        for name, (e0, e1, e2) in zip((p.name for p in w.projections), ev):
-            if w.path == "fused":
-                per_kernel[f"{name}.fused"].append(e0.elapsed_time(e2))
-            else:
-                per_kernel[f"{name}.shrink"].append(e0.elapsed_time(e1))
-                per_kernel[f"{name}.expand"].append(e1.elapsed_time(e2))
+        for (label, e0), (_, e1) in zip(marks, marks[1:]):
+            per_kernel.setdefault(label, []).append(e0.elapsed_time(e1))
     return step_ms, {k: statistics.mean(v) for k, v in per_kernel.items()}
 
 
@@ -510,7 +552,7 @@ def main():
     world, rank, local = init_distributed()
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    w = Workload(args.config, device, args.seed + rank)
+    w = Workload(args.config, device, args.seed + rank, world)
     w.path = args.path
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
     steps, warmup = args.steps, max(3, args.warmup)
@@ -520,9 +562,11 @@ def main():
     barrier(world)
     total_ms = max_over_ranks(sum(step_ms), world)
     ms_per_step = total_ms / steps
-    value = world * w.T * steps / (total_ms / 1e3)
+    # Replicas: every rank processes its own batch; tensor-parallel: the ranks share one.
+    value = (1 if w.sharded else world) * w.T * steps / (total_ms / 1e3)
     peak, peak_kind = measured_peaks()
-    dominant = max(per_kernel, key=per_kernel.get)
+    kernels = {k: v for k, v in per_kernel.items() if k.split(".")[1] in ("shrink", "expand", "fused")}
+    dominant = max(kernels, key=kernels.get)
     name, kind = dominant.split(".")
     p = next(p for p in w.projections if p.name == name)
     alg = {
@@ -540,11 +584,12 @@ def main():
         "warmup": warmup,
         "ms_per_step": ms_per_step,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if w.sharded else "weak",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": f"synthetic (seeded; BASELINE config {args.config} shapes and distributions)",
-        "config": config | {"parallelism": f"replicas{world}", "path": w.path},
+        "config": config | {"parallelism": f"tp{world}" if w.sharded else f"replicas{world}",
+                            "path": w.path},
         "hbm_gbs_step": w.bytes_per_step() / (ms_per_step * 1e-3) / 1e9,
         "bytes_per_step": w.bytes_per_step(),
         "flops_per_step": w.flops_per_step(),
@@ -571,7 +616,9 @@ def main():
             "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h,
         }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.profile:
+    if "down_proj.allreduce" in per_kernel:  # the z all-reduce, timed on its own
+        result["allreduce_us"] = max_over_ranks(per_kernel["down_proj.allreduce"], world) * 1e3
+    if rank == 0 and world == 1 and not w.sharded and not args.no_cpu_baseline and not args.profile:
         result["cpu_baseline"] = cpu_baseline(w)
     if rank == 0:
         print(json.dumps(result), flush=True)

@@ -210,6 +210,40 @@ int lf_sgmv_prefill(const void* x, int64_t x_stride, const void* a, const void* 
 int64_t lf_sgmv_prefill_workspace_floats(int64_t num_tokens, int64_t width, int32_t num_slices,
                                          int32_t capacity);
 
+/*
+ * The two halves of lf_fused_shrink_expand (same arguments, same workspace): the shrink
+ * leaves the FP32 z rows in the workspace, the expand reads them.  Between the two a
+ * caller may combine z across devices, e.g. sum it over the ranks of a row-parallel
+ * projection whose A columns are sharded (one all-reduce of the rows lf_fused_z_rows
+ * locates).  Both calls must pass the same num_tokens, width, num_slices and capacity.
+ * No counterpart in the reference, which has no tensor parallelism on this path
+ * (src/loraforge/integrations/_sglang_fleet.py:177-178 rejects TP != 1).
+ */
+int lf_sgmv_shrink(const void* x, int64_t x_stride, const void* a, const void* b,
+                   const int64_t* b_offsets, const int32_t* b_strides, void* y, int64_t y_stride,
+                   const int32_t* segment_indptr, const int32_t* segment_slots,
+                   const int32_t* token_indices, const int32_t* ranks, const float* scales,
+                   const int32_t* slice_offsets, const int32_t* segment_count, float* workspace,
+                   int64_t workspace_floats, int64_t num_tokens, int64_t width, int32_t out_width,
+                   int32_t num_slices, int32_t capacity, int32_t num_slots, int32_t max_segments,
+                   int32_t numerics, void* stream);
+int lf_sgmv_expand(const void* x, int64_t x_stride, const void* a, const void* b,
+                   const int64_t* b_offsets, const int32_t* b_strides, void* y, int64_t y_stride,
+                   const int32_t* segment_indptr, const int32_t* segment_slots,
+                   const int32_t* token_indices, const int32_t* ranks, const float* scales,
+                   const int32_t* slice_offsets, const int32_t* segment_count, float* workspace,
+                   int64_t workspace_floats, int64_t num_tokens, int64_t width, int32_t out_width,
+                   int32_t num_slices, int32_t capacity, int32_t num_slots, int32_t max_segments,
+                   int32_t numerics, void* stream);
+
+/*
+ * Where lf_sgmv_shrink leaves z in the workspace: `*row_floats` FP32 values per token
+ * row, num_tokens rows starting `*offset` floats into the workspace (row = the token's
+ * position in token_indices; columns s*r + k hold slice s, rank index k).
+ */
+int lf_fused_z_rows(int64_t num_tokens, int64_t width, int32_t num_slices, int32_t capacity,
+                    int64_t* offset, int64_t* row_floats);
+
 /* Workspace floats lf_fused_shrink_expand needs for these sizes (-1 if invalid). */
 int64_t lf_fused_workspace_floats(int64_t num_tokens, int64_t width, int32_t num_slices,
                                   int32_t capacity);

@@ -56,6 +56,15 @@ SIGNATURES = {
         _p, _i64, _p, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _i64,
         _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _p,
     ],
+    "lf_sgmv_shrink": [
+        _p, _i64, _p, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _i64,
+        _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _p,
+    ],
+    "lf_sgmv_expand": [
+        _p, _i64, _p, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _i64,
+        _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _p,
+    ],
+    "lf_fused_z_rows": [_i64, _i64, _i32, _i32, _p, _p],
     "lf_fused_shrink_expand_noalloc": [
         _p, _i64, _p, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _p,
         _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _p,
@@ -124,6 +133,14 @@ def prefill_workspace_floats(num_tokens: int, width: int, num_slices: int, capac
     if n < 0:
         raise ValueError("invalid sizes for the prefill workspace")
     return n
+
+
+def fused_z_rows(num_tokens: int, width: int, num_slices: int, capacity: int) -> tuple[int, int]:
+    """(offset, floats per row) of the z rows lf_sgmv_shrink leaves in the workspace."""
+    offset, row = ctypes.c_int64(0), ctypes.c_int64(0)
+    call("lf_fused_z_rows", num_tokens, width, num_slices, capacity, ctypes.byref(offset),
+         ctypes.byref(row))
+    return offset.value, row.value
 
 
 def device_wait_timeouts(reset: bool = False) -> int:

@@ -932,14 +932,16 @@ Scratch decode_scratch(float* region, int64_t num_tokens, int64_t width, int num
 }
 }  // namespace lfb
 
-extern "C" int lf_fused_shrink_expand(
+namespace {
+// Validates a caller-provided workspace and runs the requested phases.
+int workspace_launch(
     const void* x, int64_t x_stride, const void* a, const void* b, const int64_t* b_offsets,
     const int32_t* b_strides, void* y, int64_t y_stride, const int32_t* segment_indptr,
     const int32_t* segment_slots, const int32_t* token_indices, const int32_t* ranks,
     const float* scales, const int32_t* slice_offsets, const int32_t* segment_count,
     float* workspace, int64_t workspace_floats, int64_t num_tokens, int64_t width,
     int32_t out_width, int32_t num_slices, int32_t capacity, int32_t num_slots,
-    int32_t max_segments, int32_t numerics, void* stream) {
+    int32_t max_segments, int32_t numerics, void* stream, int phases) {
   if (num_tokens < 0 || num_tokens >= (int64_t(1) << 31) || width < 1 || width >= (int64_t(1) << 31))
     return fail(LF_E_INVALID, "fused_shrink_expand: invalid token count or width");
   if (num_slices < 1 || num_slices > kMaxSlices || capacity < 1)
@@ -953,7 +955,66 @@ extern "C" int lf_fused_shrink_expand(
   return fused_launch(x, x_stride, a, b, b_offsets, b_strides, y, y_stride, segment_indptr,
                       segment_slots, token_indices, ranks, scales, slice_offsets, segment_count,
                       scratch, num_tokens, width, out_width, num_slices, capacity, num_slots,
-                      max_segments, numerics, kSeg, stream);
+                      max_segments, numerics, kSeg, stream, phases);
+}
+}  // namespace
+
+extern "C" int lf_fused_shrink_expand(
+    const void* x, int64_t x_stride, const void* a, const void* b, const int64_t* b_offsets,
+    const int32_t* b_strides, void* y, int64_t y_stride, const int32_t* segment_indptr,
+    const int32_t* segment_slots, const int32_t* token_indices, const int32_t* ranks,
+    const float* scales, const int32_t* slice_offsets, const int32_t* segment_count,
+    float* workspace, int64_t workspace_floats, int64_t num_tokens, int64_t width,
+    int32_t out_width, int32_t num_slices, int32_t capacity, int32_t num_slots,
+    int32_t max_segments, int32_t numerics, void* stream) {
+  return workspace_launch(x, x_stride, a, b, b_offsets, b_strides, y, y_stride, segment_indptr,
+                          segment_slots, token_indices, ranks, scales, slice_offsets, segment_count,
+                          workspace, workspace_floats, num_tokens, width, out_width, num_slices,
+                          capacity, num_slots, max_segments, numerics, stream,
+                          kPhaseShrink | kPhaseExpand);
+}
+
+// The two halves of lf_fused_shrink_expand, for callers that combine z across devices
+// between them (row-parallel LoRA): z rows are left in the workspace by the shrink and
+// read by the expand; lf_fused_z_rows tells where.
+extern "C" int lf_sgmv_shrink(
+    const void* x, int64_t x_stride, const void* a, const void* b, const int64_t* b_offsets,
+    const int32_t* b_strides, void* y, int64_t y_stride, const int32_t* segment_indptr,
+    const int32_t* segment_slots, const int32_t* token_indices, const int32_t* ranks,
+    const float* scales, const int32_t* slice_offsets, const int32_t* segment_count,
+    float* workspace, int64_t workspace_floats, int64_t num_tokens, int64_t width,
+    int32_t out_width, int32_t num_slices, int32_t capacity, int32_t num_slots,
+    int32_t max_segments, int32_t numerics, void* stream) {
+  return workspace_launch(x, x_stride, a, b, b_offsets, b_strides, y, y_stride, segment_indptr,
+                          segment_slots, token_indices, ranks, scales, slice_offsets, segment_count,
+                          workspace, workspace_floats, num_tokens, width, out_width, num_slices,
+                          capacity, num_slots, max_segments, numerics, stream, kPhaseShrink);
+}
+
+extern "C" int lf_sgmv_expand(
+    const void* x, int64_t x_stride, const void* a, const void* b, const int64_t* b_offsets,
+    const int32_t* b_strides, void* y, int64_t y_stride, const int32_t* segment_indptr,
+    const int32_t* segment_slots, const int32_t* token_indices, const int32_t* ranks,
+    const float* scales, const int32_t* slice_offsets, const int32_t* segment_count,
+    float* workspace, int64_t workspace_floats, int64_t num_tokens, int64_t width,
+    int32_t out_width, int32_t num_slices, int32_t capacity, int32_t num_slots,
+    int32_t max_segments, int32_t numerics, void* stream) {
+  return workspace_launch(x, x_stride, a, b, b_offsets, b_strides, y, y_stride, segment_indptr,
+                          segment_slots, token_indices, ranks, scales, slice_offsets, segment_count,
+                          workspace, workspace_floats, num_tokens, width, out_width, num_slices,
+                          capacity, num_slots, max_segments, numerics, stream, kPhaseExpand);
+}
+
+extern "C" int lf_fused_z_rows(int64_t num_tokens, int64_t width, int32_t num_slices,
+                               int32_t capacity, int64_t* offset, int64_t* row_floats) {
+  if (num_tokens < 0 || width < 1 || num_slices < 1 || num_slices > kMaxSlices || capacity < 1 ||
+      !offset || !row_floats)
+    return fail(LF_E_INVALID, "fused_z_rows: invalid sizes");
+  const ShrinkConfig sc = shrink_config(width, num_slices, capacity);
+  const int64_t T = num_tokens > 0 ? num_tokens : 1;
+  *offset = int64_t(sc.nchunks) * T * sc.rstride;
+  *row_floats = sc.rstride;
+  return LF_OK;
 }
 
 namespace lfb {
@@ -964,7 +1025,7 @@ int fused_launch(const void* x, int64_t x_stride, const void* a, const void* b,
                  const int32_t* slice_offsets, const int32_t* segment_count, const Scratch& scratch,
                  int64_t num_tokens, int64_t width, int32_t out_width, int32_t num_slices,
                  int32_t capacity, int32_t num_slots, int32_t max_segments, int32_t numerics,
-                 int max_tokens, void* stream) {
+                 int max_tokens, void* stream, int phases) {
   if (num_tokens < 0 || num_tokens >= (int64_t(1) << 31) || width < 1 || width >= (int64_t(1) << 31))
     return fail(LF_E_INVALID, "fused_shrink_expand: invalid token count or width");
   if (out_width < 1 || num_slices < 1 || num_slices > kMaxSlices || capacity < 1 || num_slots < 1)
@@ -1011,7 +1072,7 @@ int fused_launch(const void* x, int64_t x_stride, const void* a, const void* b,
   if (seg_cap * sc.nchunks >= (int64_t(1) << 31) ||
       seg_cap * ((out_width + kExpandCols - 1) / kExpandCols) >= (int64_t(1) << 31))
     return fail(LF_E_INVALID, "fused_shrink_expand: too many (segment, chunk) units");
-  {
+  if (phases & kPhaseShrink) {
     // Up to 8 n tiles (S*r <= 64) the warps accumulate in registers.
     const bool regs = sc.rstride <= 64;
     auto shrink = regs ? sgmv_shrink_kernel<true> : sgmv_shrink_kernel<false>;
@@ -1022,6 +1083,7 @@ int fused_launch(const void* x, int64_t x_stride, const void* a, const void* b,
     const int grid = int(units < ctas ? units : ctas);
     if (int rc = launch_pdl(shrink, grid, sc.smem, s, p, "fused_shrink_expand (shrink)")) return rc;
   }
+  if (!(phases & kPhaseExpand)) return LF_OK;
   p.stages = ec.stages;
   p.stage_bytes = ec.stage_bytes;
   const int64_t units = seg_cap * ((out_width + kExpandCols - 1) / kExpandCols);
@@ -1115,5 +1177,5 @@ extern "C" int lf_fused_shrink_expand_noalloc(
   return fused_launch(x, x_stride, a, b, b_offsets, b_strides, y, y_stride, segment_indptr,
                       segment_slots, token_indices, ranks, scales, slice_offsets, segment_count,
                       scratch, num_tokens, width, out_width, num_slices, capacity, num_slots,
-                      max_segments, numerics, kSeg, stream);
+                      max_segments, numerics, kSeg, stream, kPhaseShrink | kPhaseExpand);
 }

@@ -6,6 +6,8 @@
 
 namespace lfb {
 
+enum FusedPhase { kPhaseShrink = 1, kPhaseExpand = 2 };
+
 // Scratch of one decode shrink -> expand call: FP32 partials and z rows (every value
 // read is written earlier in the same call) and one completion counter per segment
 // (zero before the first call; every call leaves the counters it used at zero).
@@ -30,7 +32,7 @@ int fused_launch(const void* x, int64_t x_stride, const void* a, const void* b,
                  const int32_t* slice_offsets, const int32_t* segment_count, const Scratch& scratch,
                  int64_t num_tokens, int64_t width, int32_t out_width, int32_t num_slices,
                  int32_t capacity, int32_t num_slots, int32_t max_segments, int32_t numerics,
-                 int max_tokens, void* stream);
+                 int max_tokens, void* stream, int phases);
 
 // Expired bounded waits counted by the prefill kernels' translation unit (synchronous).
 int prefill_wait_timeouts(unsigned int* value, int reset);

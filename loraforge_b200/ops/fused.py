@@ -213,3 +213,47 @@ def _launch(entry, sizer, x, a, b, output, b_offsets, b_strides, ranks, scales,
             NUMERICS[numerics],
             _native.stream_of(x.device),
         )
+
+
+def sgmv_shrink(x, a, b, output, *, workspace, **routing) -> None:
+    """First half of ``lora_shrink_expand``: z = A_g @ x[t] into ``workspace``.
+
+    Same keyword arguments as ``lora_shrink_expand`` (``output`` and B are validated
+    but not touched).  The FP32 z rows stay in ``workspace`` (see ``z_rows``) until
+    ``sgmv_expand`` consumes them; pass the same workspace and sizes to both.
+    """
+    if workspace is None:
+        raise ValueError("sgmv_shrink needs a caller-owned workspace that outlives the call")
+    _launch_routed("lf_sgmv_shrink", x, a, b, output, workspace, routing)
+
+
+def sgmv_expand(x, a, b, output, *, workspace, **routing) -> None:
+    """Second half of ``lora_shrink_expand``: output += scale * B_g @ z from ``workspace``."""
+    if workspace is None:
+        raise ValueError("sgmv_expand needs the workspace sgmv_shrink wrote")
+    _launch_routed("lf_sgmv_expand", x, a, b, output, workspace, routing)
+
+
+def z_rows(workspace, tokens: int, width: int, num_slices: int, capacity: int):
+    """View of the FP32 z rows ``sgmv_shrink`` leaves in ``workspace``: [tokens, row].
+
+    Row t belongs to the token at position t of ``token_indices``; columns s*r + k hold
+    slice s, rank index k.  Summing this view over the ranks of a row-parallel
+    projection (A columns sharded) between ``sgmv_shrink`` and ``sgmv_expand`` gives
+    every rank the full z.
+    """
+    offset, row = _native.fused_z_rows(tokens, width, num_slices, capacity)
+    return workspace[offset : offset + max(tokens, 1) * row].view(max(tokens, 1), row)[:tokens]
+
+
+def _launch_routed(entry, x, a, b, output, workspace, routing):
+    routing = dict(routing)
+    num_slices = routing.pop("num_slices", 1)
+    numerics = routing.pop("numerics", "fp32")
+    keys = ("b_offsets", "b_strides", "ranks", "scales", "segment_indptr", "segment_slots",
+            "token_indices", "slice_offsets", "segment_count")
+    missing = [k for k in keys if k not in routing]
+    if missing or set(routing) - set(keys):
+        raise TypeError(f"expected keyword arguments {keys}")
+    _launch(entry, _native.fused_workspace_floats, x, a, b, output, *(routing[k] for k in keys),
+            num_slices, numerics, workspace)
