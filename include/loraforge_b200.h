@@ -55,6 +55,20 @@ int lf_group_tokens(const int32_t* slots, int64_t num_tokens, int32_t num_slots,
                     int32_t* token_indices, int32_t* segment_count, void* stream);
 
 /*
+ * Inverse of the grouping: routes[t] = the slot of the segment whose token_indices range
+ * holds t, -1 for tokens in no segment.  Reads *segment_count on the device (segments
+ * beyond it or beyond max_segments, index entries outside [0, num_indices) and
+ * positions outside [0, num_tokens) are ignored), so it turns a serving framework's
+ * segment table (SGLang's seg_indptr / weight_indices / permutation, consumed by the
+ * reference at src/loraforge/integrations/_sglang_fleet.py:390-407) into the
+ * per-token slots the row-form shrink takes, inside a captured graph.
+ */
+int lf_segment_routes(const int32_t* segment_indptr, const int32_t* segment_slots,
+                      const int32_t* token_indices, const int32_t* segment_count,
+                      int32_t max_segments, int64_t num_indices, int64_t num_tokens,
+                      int32_t* routes, void* stream);
+
+/*
  * Retained-rank BF16 shrink: z[t, s*r+k] = bf16(sum_i a[g, s*r+k, i] * x[t, i]) for
  * g = slots[t] >= 0, r = ranks[g] in 1..max_rank, s < num_slices, k < r.  Other z
  * entries are left unchanged.  x row stride `x_stride` (elements), A contiguous

@@ -70,6 +70,7 @@ SIGNATURES = {
         _i64, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _p,
     ],
     "lf_device_wait_timeouts": [_p, _i32],
+    "lf_segment_routes": [_p, _p, _p, _p, _i32, _i64, _i64, _p, _p],
 }
 
 _lock = threading.Lock()

@@ -189,8 +189,56 @@ group_tokens_kernel(const int32_t* __restrict__ slots, int T, int num_slots, int
   }
 }
 
+// routes[token_indices[i]] = segment_slots[s] for every i in segment s's range; one warp
+// per segment, grid-stride over segments.  Segments past *segment_count (or
+// max_segments), index entries outside [0, num_indices) and token positions outside
+// [0, T) are ignored, so padded routing tables of captured graphs are safe.
+__global__ void segment_routes_kernel(const int32_t* __restrict__ indptr,
+                                      const int32_t* __restrict__ seg_slots,
+                                      const int32_t* __restrict__ token_indices,
+                                      const int32_t* __restrict__ segment_count,
+                                      int max_segments, int num_indices, int T,
+                                      int32_t* __restrict__ routes) {
+  const int lane = threadIdx.x & 31;
+  const int nseg = min(max_segments, max(0, *segment_count));
+  const int warps = gridDim.x * (blockDim.x >> 5);
+  for (int s = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); s < nseg; s += warps) {
+    const int begin = max(0, indptr[s]), end = min(num_indices, indptr[s + 1]);
+    const int slot = seg_slots[s];
+    for (int i = begin + lane; i < end; i += 32) {
+      const int t = token_indices[i];
+      if (t >= 0 && t < T) routes[t] = slot;
+    }
+  }
+}
+
 }  // namespace
 }  // namespace lfb
+
+extern "C" int lf_segment_routes(const int32_t* segment_indptr, const int32_t* segment_slots,
+                                 const int32_t* token_indices, const int32_t* segment_count,
+                                 int32_t max_segments, int64_t num_indices, int64_t num_tokens,
+                                 int32_t* routes, void* stream) {
+  using namespace lfb;
+  if (num_tokens < 0 || num_tokens >= (int64_t(1) << 31) || num_indices < 0 ||
+      num_indices >= (int64_t(1) << 31) || max_segments < 0)
+    return fail(LF_E_INVALID, "segment_routes: sizes must fit signed int32");
+  if (num_tokens == 0) return LF_OK;
+  if (!routes || !segment_count || (max_segments && (!segment_indptr || !segment_slots)) ||
+      (num_indices && !token_indices))
+    return fail(LF_E_INVALID, "segment_routes: null buffer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // 0xff bytes make every int32 route -1 (no adapter) before the scatter.
+  if (cudaMemsetAsync(routes, 0xff, sizeof(int32_t) * size_t(num_tokens), s) != cudaSuccess)
+    return check_launch("segment_routes memset");
+  if (max_segments == 0) return LF_OK;
+  const int threads = 256, per_block = threads / 32;
+  const int blocks = min((max_segments + per_block - 1) / per_block, 4 * 148);
+  segment_routes_kernel<<<blocks, threads, 0, s>>>(segment_indptr, segment_slots, token_indices,
+                                                  segment_count, max_segments, int(num_indices),
+                                                  int(num_tokens), routes);
+  return check_launch("segment_routes");
+}
 
 extern "C" int lf_group_tokens(const int32_t* slots, int64_t num_tokens, int32_t num_slots,
                                int32_t chunk, int32_t* segment_indptr,

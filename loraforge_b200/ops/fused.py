@@ -63,6 +63,10 @@ def lora_shrink_expand(
     allocation-free).  A caller-owned workspace must be zero-filled before its
     first use (``torch.zeros``); every call leaves its counters at zero again, so
     one workspace serves any sequence of calls of the same sizes on one stream.
+    ``workspace="builtin"`` uses the library's fixed per-device scratch instead
+    (``lf_fused_shrink_expand_noalloc``: up to 16384 tokens, any sequence of sizes,
+    no allocation, so serving graphs of every batch size can share it); calls that
+    use it must not run concurrently on different streams of one device.
     """
     _launch(
         "lf_fused_shrink_expand", _native.fused_workspace_floats, x, a, b, output, b_offsets,
@@ -166,6 +170,22 @@ def _launch(entry, sizer, x, a, b, output, b_offsets, b_strides, ranks, scales,
          token_indices, slice_offsets, segment_count),
     )
     capacity = a.shape[1] // num_slices
+    if isinstance(workspace, str):
+        if workspace != "builtin" or entry != "lf_fused_shrink_expand":
+            raise ValueError("workspace='builtin' applies to lora_shrink_expand only")
+        if x.shape[0] == 0:
+            return
+        with torch.cuda.device(x.device):
+            _native.call(
+                "lf_fused_shrink_expand_noalloc", x.data_ptr(), x.stride(0), a.data_ptr(),
+                b.data_ptr(), b_offsets.data_ptr(), b_strides.data_ptr(), output.data_ptr(),
+                output.stride(0), segment_indptr.data_ptr(), segment_slots.data_ptr(),
+                token_indices.data_ptr(), ranks.data_ptr(), scales.data_ptr(),
+                slice_offsets.data_ptr(), segment_count.data_ptr(), x.shape[0], x.shape[1],
+                output.shape[1], num_slices, capacity, nslots, segment_slots.numel(),
+                NUMERICS[numerics], _native.stream_of(x.device),
+            )
+        return
     need = sizer(x.shape[0], x.shape[1], num_slices, capacity)
     if workspace is None:
         workspace = torch.zeros(need, dtype=torch.float32, device=x.device)

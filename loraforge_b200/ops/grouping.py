@@ -78,3 +78,39 @@ def group_tokens(slots, num_slots: int, *, chunk: int = 16, out: Routing | None 
             _native.stream_of(slots.device),
         )
     return out
+
+
+def segment_routes(segment_indptr, segment_slots, token_indices, segment_count, num_tokens: int, *, out=None):
+    """Per-token slots (int32 [num_tokens], -1 = none) from a segment table.
+
+    The inverse of ``group_tokens``: token ``token_indices[i]`` for ``i`` in segment
+    s's range gets ``segment_slots[s]``.  ``segment_count`` (int32, on the device) is
+    read by the kernel, so padded tables of captured graphs work unchanged.
+    """
+    import torch
+
+    for t, name in ((segment_indptr, "segment_indptr"), (segment_slots, "segment_slots"),
+                    (token_indices, "token_indices"), (segment_count, "segment_count")):
+        if not isinstance(t, torch.Tensor):
+            raise TypeError(f"{name} must be a torch.Tensor")
+        if t.ndim != 1 and not (name == "segment_count" and t.ndim == 0):
+            raise ValueError(f"{name} must be a vector")
+        if t.dtype != torch.int32 or not t.is_contiguous() or t.device != segment_indptr.device:
+            raise ValueError(f"{name} must be a contiguous int32 tensor on the routing device")
+    if segment_indptr.device.type != "cuda":
+        raise ValueError("routing tables must be on a CUDA device")
+    if segment_indptr.numel() < segment_slots.numel() + 1:
+        raise ValueError("segment_indptr needs one more entry than segment_slots")
+    if type(num_tokens) is not int or num_tokens < 0:
+        raise ValueError("num_tokens must be a nonnegative integer")
+    if out is None:
+        out = torch.empty(num_tokens, dtype=torch.int32, device=segment_indptr.device)
+    elif out.dtype != torch.int32 or not out.is_contiguous() or out.numel() < num_tokens or out.device != segment_indptr.device:
+        raise ValueError("out must be a contiguous int32 buffer with room for every token")
+    with torch.cuda.device(segment_indptr.device):
+        _native.call(
+            "lf_segment_routes", segment_indptr.data_ptr(), segment_slots.data_ptr(),
+            token_indices.data_ptr(), segment_count.data_ptr(), segment_slots.numel(),
+            token_indices.numel(), num_tokens, out.data_ptr(), _native.stream_of(segment_indptr.device),
+        )
+    return out[:num_tokens]

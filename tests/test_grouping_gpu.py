@@ -81,3 +81,34 @@ def test_graph_capture_replays_with_new_routes():
         assert out.segment_count.item() == count
         assert out.token_indices.tolist() == perm.tolist()
         assert out.segment_slots[:count].tolist() == seg_slots.tolist()
+
+
+@pytest.mark.parametrize("chunk", [1, 16, 128])
+def test_segment_routes_inverts_grouping(chunk):
+    from loraforge_b200.ops.grouping import segment_routes
+
+    rng = np.random.default_rng(chunk)
+    slots_np = rng.integers(-1, 40, size=3000).astype(np.int32)
+    slots = torch.from_numpy(slots_np).cuda()
+    routing = group_tokens(slots, 40, chunk=chunk)
+    routes = segment_routes(*routing, len(slots_np))
+    torch.cuda.synchronize()
+    # Grouping skips inactive tokens and slots outside [0, num_slots); they come back as -1.
+    assert routes.cpu().numpy().tolist() == np.where(slots_np >= 0, slots_np, -1).tolist()
+
+
+def test_segment_routes_ignores_padded_segments():
+    from loraforge_b200.ops.grouping import segment_routes
+
+    # Two live segments, then padding whose ranges point past the token table.
+    indptr = torch.tensor([0, 2, 3, 9, 9], dtype=torch.int32, device="cuda")
+    seg_slots = torch.tensor([5, 7, 9, 9], dtype=torch.int32, device="cuda")
+    perm = torch.tensor([3, 0, 1], dtype=torch.int32, device="cuda")
+    count = torch.tensor([2], dtype=torch.int32, device="cuda")
+    routes = segment_routes(indptr, seg_slots, perm, count, 5)
+    torch.cuda.synchronize()
+    assert routes.tolist() == [5, 7, -1, 5, -1]
+    count.fill_(4)  # padded segments now counted: their index range is clipped to the table
+    routes = segment_routes(indptr, seg_slots, perm, count, 5)
+    torch.cuda.synchronize()
+    assert routes.tolist() == [5, 7, -1, 5, -1]

@@ -101,3 +101,31 @@ def test_rejects_sizes_beyond_the_built_in_buffer():
             big_tokens, x.shape[1], base.shape[1], S, rank, meta["ranks"].numel(),
             meta["segment_slots"].numel(), 0, _native.stream_of(x.device),
         )
+
+
+def test_builtin_workspace_keyword_in_captured_graphs_of_two_sizes():
+    # Serving graphs of different batch sizes share the built-in scratch.
+    cases = [make_case(seed, tokens=tokens) for seed, tokens in ((5, 64), (6, 200))]
+    expected, outs, graphs = [], [], []
+    for x, a, b, base, meta, S, rank in cases:
+        want = base.clone()
+        lora_shrink_expand(x, a, b, want, **meta, num_slices=S)
+        expected.append(want)
+        out = base.clone()
+        lora_shrink_expand(x, a, b, out, **meta, num_slices=S, workspace="builtin")  # warm outside capture
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            lora_shrink_expand(x, a, b, out, **meta, num_slices=S, workspace="builtin")
+        outs.append(out)
+        graphs.append(graph)
+    for _ in range(2):
+        for (x, a, b, base, meta, S, rank), out, graph in zip(cases, outs, graphs):
+            out.copy_(base)
+            graph.replay()
+    torch.cuda.synchronize()
+    for out, want in zip(outs, expected):
+        torch.testing.assert_close(out, want, rtol=0, atol=0)
+    x, a, b, base, meta, S, rank = cases[0]
+    with pytest.raises(ValueError, match="builtin"):
+        lora_shrink_expand(x, a, b, base.clone(), **meta, num_slices=S, workspace="static")
+    assert _native.device_wait_timeouts(reset=True) == 0
