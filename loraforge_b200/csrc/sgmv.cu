@@ -282,9 +282,19 @@ __device__ __forceinline__ void publish_run(const Params& p, int* flag, int tid,
     for (int e = tid; e < n * R; e += kConsumers) {
       const int m = e / R, j = e - m * R;
       const float* src = p.partial + int64_t(pos0 + m) * p.rstride + j;
+      // Runs in chunk order; up to eight partials are loaded before they are added, so
+      // their L2 round trips overlap (the order of the additions does not change).
       float s = 0.f;
-      for (int c = 0; c < p.nchunks; c = ((seg_first + c) / per + 1) * per - seg_first)
-        s += __ldcg(src + c * cstride);
+      for (int c = 0; c < p.nchunks;) {
+        float v[8];
+        int cs[8], k = 0;
+        for (; k < 8 && c < p.nchunks; ++k, c = ((seg_first + c) / per + 1) * per - seg_first) cs[k] = c;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = i < k ? __ldcg(src + cs[i] * cstride) : 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (i < k) s += v[i];
+      }
       p.zfinal[int64_t(pos0 + m) * p.rstride + j] = s;
     }
     if (tid == 0) p.counters[seg] = 0;
@@ -316,6 +326,9 @@ __global__ void __launch_bounds__(kThreads, REGS ? 2 : 1)
   }
   if (!REGS)
     for (int i = tid; i < kSeg * p.rstride; i += kThreads) acc[i] = 0.f;
+  // The A tensor map lives in kernel parameter space: fetch it while the preceding grid
+  // finishes, so the first TMA issue does not wait for it.
+  if (tid == kConsumers) asm volatile("prefetch.tensormap [%0];" ::"l"(&p.tmap_a) : "memory");
   __syncthreads();
   pdl_wait();  // x, metadata and the workspace may come from the preceding grid
   pdl_launch_dependents();
@@ -519,33 +532,40 @@ __device__ __forceinline__ int slice_of(const int* offs, int S, int col) {
 }
 
 // z fragments of slice s for this lane, multiplied by `mul`: [mma q][hi, lo][4 regs].
+// Every z value of the lane is loaded before the first is converted, so the loads
+// overlap instead of paying one L2 round trip each.
 template <int KP, int MODE>
 __device__ __forceinline__ void load_z(const Params& p, const ExpandHeader& h, int s, float mul,
                                        int g, int t, uint32_t (&zf)[4][2][4]) {
   const int live = min(h.r, h.bucket);
-  auto zv = [&](int m, int kk) -> float {
-    return (m < h.n && kk < live)
-               ? mul * __ldcg(p.zfinal + int64_t(h.pos0 + m) * p.rstride + s * h.r + kk)
-               : 0.f;
-  };
-  auto put = [&](int q, int reg, float v0, float v1) {
+  constexpr int NV = KP == 8 ? 4 : KP / 16 * 8;
+  const float* zr0 = p.zfinal + int64_t(h.pos0 + g) * p.rstride + s * h.r;
+  const float* zr1 = zr0 + int64_t(8) * p.rstride;
+  float v[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    // Value i: row half m (token g or g + 8) and rank index kk of fragment register
+    // i / 2 of MMA i / 8, in the k order the B fragments use.
+    int m, kk;
+    if constexpr (KP == 8) {
+      m = i >> 1;
+      kk = 2 * t + (i & 1);
+    } else {
+      const int q = i >> 3, j = i & 7;
+      const int base = KP == 16 ? 4 * t : 32 * (q >> 1) + 8 * t + 4 * (q & 1);
+      m = (j >> 1) & 1;
+      kk = base + ((j >> 2) << 1) + (j & 1);
+    }
+    v[i] = (g + 8 * m < h.n && kk < live) ? __ldcg((m ? zr1 : zr0) + kk) : 0.f;
+  }
+#pragma unroll
+  for (int i = 0; i < NV; i += 2) {
+    const int q = KP == 8 ? 0 : i >> 3, reg = KP == 8 ? i >> 1 : (i & 7) >> 1;
+    const float v0 = mul * v[i], v1 = mul * v[i + 1];
     if (MODE == kFp32) {
       split2(v0, v1, zf[q][0][reg], zf[q][1][reg]);
     } else {
       zf[q][0][reg] = pack2(float_to_bf16_bits(v0), float_to_bf16_bits(v1));
-    }
-  };
-  if constexpr (KP == 8) {
-    put(0, 0, zv(g, 2 * t), zv(g, 2 * t + 1));
-    put(0, 1, zv(g + 8, 2 * t), zv(g + 8, 2 * t + 1));
-  } else {
-#pragma unroll
-    for (int q = 0; q < KP / 16; ++q) {
-      const int base = KP == 16 ? 4 * t : 32 * (q >> 1) + 8 * t + 4 * (q & 1);
-      put(q, 0, zv(g, base), zv(g, base + 1));
-      put(q, 1, zv(g + 8, base), zv(g + 8, base + 1));
-      put(q, 2, zv(g, base + 2), zv(g, base + 3));
-      put(q, 3, zv(g + 8, base + 2), zv(g + 8, base + 3));
     }
   }
 }
@@ -686,6 +706,86 @@ __device__ __forceinline__ void expand_stage(const Params& p, const ExpandHeader
   }
 }
 
+// Stages whose columns lie in one slice, with y staged and bucket <= 16: each warp runs
+// two of its 32-column groups side by side (same arithmetic as expand_stage), so the y
+// loads, MMA chains and stores of one group overlap the latencies of the other.
+template <int KP, int MODE>
+__device__ __forceinline__ void expand_stage_pair(const Params& p, const ExpandHeader& h,
+                                                  const uint8_t* st, uint32_t (&zf)[4][2][4],
+                                                  int& zseg, int& zslice, int lane, int warp) {
+  constexpr int PARTS = MODE == kFp32 ? 2 : 1;
+  const int g = lane >> 2, t = lane & 3;
+  const float mul = MODE == kFp32 ? h.scale : 1.f;  // fp32: scale folded into z
+  if (h.seg != zseg || h.slice != zslice) {
+    load_z<KP, MODE>(p, h, h.slice, mul, g, t, zf);
+    zseg = h.seg;
+    zslice = h.slice;
+  }
+  const int groups = (h.ncols + 31) >> 5;
+  for (int grp0 = warp; grp0 < groups; grp0 += 2 * kConsumerWarps) {
+    float d[2][4][4];
+    int my[2];
+    bool mine[2];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      my[q] = (grp0 + q * kConsumerWarps) * 32 + 8 * t;
+      mine[q] = my[q] < h.ncols;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int m = g + 8 * hh;
+        float v[8];
+        uint4 w = make_uint4(0, 0, 0, 0);
+        if (MODE == kFp32 && mine[q] && m < h.n) w = lds16(st + kBStage + m * kYStagePitch + my[q] * 2);
+        unpack_bf16x8(w, v);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          d[q][j][2 * hh] = v[2 * j];
+          d[q][j][2 * hh + 1] = v[2 * j + 1];
+        }
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      if (grp0 + q * kConsumerWarps >= groups) break;
+      const int c_rel = (grp0 + q * kConsumerWarps) * 32;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint32_t bf[4][2];
+        load_b<KP>(st, c_rel + 8 * (g >> 1) + 2 * j + (g & 1), h.bucket, t, bf);
+#pragma unroll
+        for (int part = 0; part < PARTS; ++part) {
+          if constexpr (KP == 8) {
+            mma1688(d[q][j], zf[0][part][0], zf[0][part][1], bf[0][0]);
+          } else {
+            mma16816(d[q][j], zf[0][part][0], zf[0][part][1], zf[0][part][2], zf[0][part][3], bf[0][0],
+                     bf[0][1]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        const int m = g + 8 * hh;
+        if (m >= h.n || !mine[q]) continue;
+        float v[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) v[c] = d[q][c >> 1][2 * hh + (c & 1)];
+        if (MODE != kFp32) {
+          float yv[8];
+          unpack_bf16x8(lds16(st + kBStage + m * kYStagePitch + my[q] * 2), yv);
+#pragma unroll
+          for (int c = 0; c < 8; ++c) v[c] = yv[c] + round_through_bf16(v[c] * h.scale);
+        }
+        uint16_t* yrow = p.y + int64_t(h.tok[m]) * p.y_stride + h.col0 + my[q];
+        *reinterpret_cast<uint4*>(yrow) = make_uint4(cvt_bf16x2(v[0], v[1]), cvt_bf16x2(v[2], v[3]),
+                                                     cvt_bf16x2(v[4], v[5]), cvt_bf16x2(v[6], v[7]));
+      }
+    }
+  }
+}
+
 template <int MODE, bool STAGED>
 __global__ void __launch_bounds__(kThreads, 2) sgmv_expand_kernel(const __grid_constant__ Params p) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -805,7 +905,10 @@ __global__ void __launch_bounds__(kThreads, 2) sgmv_expand_kernel(const __grid_c
     const uint8_t* st = smem + stage * SB;
     const ExpandHeader& h = *reinterpret_cast<const ExpandHeader*>(st + hoff);
     if (h.ok < 0) break;
-    switch (h.bucket < 8 ? 8 : h.bucket) {
+    if (STAGED && h.slice >= 0 && h.bucket <= 16) {
+      if (h.bucket == 16) expand_stage_pair<16, MODE>(p, h, st, zf, zseg, zslice, lane, warp);
+      else expand_stage_pair<8, MODE>(p, h, st, zf, zseg, zslice, lane, warp);
+    } else switch (h.bucket < 8 ? 8 : h.bucket) {
       case 8: expand_stage<8, MODE, STAGED>(p, h, st, offs, zf, zseg, zslice, lane, warp); break;
       case 16: expand_stage<16, MODE, STAGED>(p, h, st, offs, zf, zseg, zslice, lane, warp); break;
       case 32: expand_stage<32, MODE, STAGED>(p, h, st, offs, zf, zseg, zslice, lane, warp); break;
