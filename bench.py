@@ -60,6 +60,8 @@ def parse_args():
     p.add_argument("--config", type=int, choices=sorted(CONFIGS), default=1)
     p.add_argument("--seed", type=int, default=1234)
     p.add_argument("--path", choices=("fused", "rows"), default="fused")
+    p.add_argument("--allreduce", choices=("peer", "nccl"), default="peer",
+                   help="tensor-parallel z sum: one kernel over NVLink peer memory, or NCCL")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--profile", action="store_true", help="short run for ncu (no sampling/baselines)")
@@ -280,7 +282,11 @@ def run_step(w, mark=None):
                 import torch.distributed as dist
 
                 mark(f"{p.name}.allreduce")
-                dist.all_reduce(z_rows(p.workspace, w.T, p.K, p.S, p.cap))
+                z = z_rows(p.workspace, w.T, p.K, p.S, p.cap)
+                if getattr(w, "peer", None) is not None:
+                    w.peer(z)
+                else:
+                    dist.all_reduce(z)
             mark(f"{p.name}.expand")
             sgmv_expand(x, p.a, p.b, p.y, workspace=p.workspace, **meta, num_slices=p.S)
         elif w.path == "fused":
@@ -554,6 +560,13 @@ def main():
     torch.cuda.set_device(device)
     w = Workload(args.config, device, args.seed + rank, world)
     w.path = args.path
+    w.peer = None
+    if w.sharded and world > 1 and args.allreduce == "peer":
+        from loraforge_b200.ops.fused import z_rows
+        from loraforge_b200.ops.sharded import PeerAllReduce
+
+        down = next(p for p in w.projections if p.name == "down_proj")
+        w.peer = PeerAllReduce(z_rows(down.workspace, w.T, down.K, down.S, down.cap).numel(), device=device)
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=device)
     steps, warmup = args.steps, max(3, args.warmup)
     barrier(world)
@@ -589,7 +602,8 @@ def main():
         "dtype": "bf16",
         "data": f"synthetic (seeded; BASELINE config {args.config} shapes and distributions)",
         "config": config | {"parallelism": f"tp{world}" if w.sharded else f"replicas{world}",
-                            "path": w.path},
+                            "path": w.path}
+                  | ({"z_allreduce": args.allreduce} if w.sharded and world > 1 else {}),
         "hbm_gbs_step": w.bytes_per_step() / (ms_per_step * 1e-3) / 1e9,
         "bytes_per_step": w.bytes_per_step(),
         "flops_per_step": w.flops_per_step(),
@@ -622,6 +636,8 @@ def main():
         result["cpu_baseline"] = cpu_baseline(w)
     if rank == 0:
         print(json.dumps(result), flush=True)
+    if w.peer is not None:
+        w.peer.close()
     if world > 1:
         import torch.distributed as dist
 

@@ -294,6 +294,34 @@ int lf_fused_shrink_expand_noalloc(const void* x, int64_t x_stride, const void* 
                                    int32_t numerics, void* stream);
 
 /*
+ * Symmetric buffers and a one-shot sum over NVLink peer memory, for the row-parallel
+ * LoRA intermediate (the all-reduce of the FP32 z rows between sgmv_shrink and
+ * sgmv_expand; the reference has no tensor-parallel path, src/loraforge/integrations/
+ * _sglang_fleet.py:177-178 rejects TP != 1).  Set-up, once per rank and device (these
+ * allocate and map; the sum does not):
+ *   lf_peer_alloc      cudaMalloc a buffer of lf_peer_buffer_bytes(capacity_floats) bytes,
+ *                      zero it, and write its CUDA IPC handle (lf_peer_handle_bytes() bytes);
+ *   lf_peer_open       map a peer rank's handle into this process (cudaIpcOpenMemHandle);
+ *   lf_peer_close / lf_peer_free  undo them (after every rank's last lf_peer_sum).
+ * lf_peer_sum: `bases` is a device array of `world` buffer pointers in rank order (this
+ * rank's own buffer at `rank`, the mapped peers elsewhere); every rank calls it with its
+ * own z (floats <= capacity_floats FP32 values, 16-byte aligned) in the same order on its
+ * stream, and on return every rank's z holds the sum over ranks, added in rank order (the
+ * same bits on every rank).  One launch of 16 CTAs; the epoch lives on the device, so the
+ * call may be captured in a CUDA graph.  Waits for peers are bounded (well under 2 s); on
+ * expiry z keeps this rank's partial and lf_peer_status reports 1.
+ */
+int64_t lf_peer_buffer_bytes(int64_t capacity_floats);
+int lf_peer_handle_bytes(void);
+int lf_peer_alloc(int64_t capacity_floats, void** buffer, void* ipc_handle);
+int lf_peer_open(const void* ipc_handle, void** buffer);
+int lf_peer_close(void* buffer);
+int lf_peer_free(void* buffer);
+int lf_peer_status(void* own_buffer, int32_t* status, int32_t reset);
+int lf_peer_sum(const uint64_t* bases, int32_t rank, int32_t world, float* z, int64_t floats,
+                int64_t capacity_floats, void* stream);
+
+/*
  * Number of bounded device-side waits (mbarrier polls in the bulk-copy kernels)
  * that expired since the last reset; a non-zero count means a kernel gave up and
  * skipped work instead of hanging.  Synchronous; reset != 0 clears the counter.

@@ -71,6 +71,12 @@ SIGNATURES = {
     ],
     "lf_device_wait_timeouts": [_p, _i32],
     "lf_segment_routes": [_p, _p, _p, _p, _i32, _i64, _i64, _p, _p],
+    "lf_peer_alloc": [_i64, _p, _p],
+    "lf_peer_open": [_p, _p],
+    "lf_peer_close": [_p],
+    "lf_peer_free": [_p],
+    "lf_peer_status": [_p, _p, _i32],
+    "lf_peer_sum": [_p, _i32, _i32, _p, _i64, _i64, _p],
 }
 
 _lock = threading.Lock()
@@ -80,7 +86,8 @@ _lib = None
 def exported_symbols() -> tuple[str, ...]:
     """Every symbol the header declares (checked by the CPU test suite)."""
     return ("lf_version", "lf_last_error_string", "lf_fused_workspace_floats",
-            "lf_sgmv_prefill_workspace_floats", *SIGNATURES)
+            "lf_sgmv_prefill_workspace_floats", "lf_peer_buffer_bytes", "lf_peer_handle_bytes",
+            *SIGNATURES)
 
 
 def library() -> ctypes.CDLL:
@@ -107,6 +114,10 @@ def library() -> ctypes.CDLL:
             for sizer in ("lf_fused_workspace_floats", "lf_sgmv_prefill_workspace_floats"):
                 getattr(lib, sizer).restype = ctypes.c_int64
                 getattr(lib, sizer).argtypes = [_i64, _i64, _i32, _i32]
+            lib.lf_peer_buffer_bytes.restype = ctypes.c_int64
+            lib.lf_peer_buffer_bytes.argtypes = [_i64]
+            lib.lf_peer_handle_bytes.restype = ctypes.c_int
+            lib.lf_peer_handle_bytes.argtypes = []
             _lib = lib
     return _lib
 
