@@ -266,7 +266,7 @@ def run_step(w, mark=None):
     mark = mark or (lambda label: None)
     prefill = w.prefill and w.path == "fused"
     fused_op = lora_shrink_expand_prefill if prefill else lora_shrink_expand
-    r = group_tokens(w.slots, w.nslots, chunk=128 if prefill else 16, out=w.routing)
+    r = group_tokens(w.slots, w.nslots, chunk=128 if prefill else 16, runs=prefill, out=w.routing)
     routing = dict(
         segment_indptr=r.segment_indptr, segment_slots=r.segment_slots,
         token_indices=r.token_indices, segment_count=r.segment_count,

@@ -55,6 +55,21 @@ int lf_group_tokens(const int32_t* slots, int64_t num_tokens, int32_t num_slots,
                     int32_t* token_indices, int32_t* segment_count, void* stream);
 
 /*
+ * Re-chunks a grouping (lf_group_tokens' tables) so that no segment spans a gap in token
+ * order: inside each slot's range of token_indices, every maximal run of consecutive
+ * tokens is cut into pieces of at most `chunk` tokens from its own start (chunk <= 0:
+ * one piece per run).  token_indices is unchanged; out_indptr [T+1], out_slots [T] and
+ * out_count [1] receive the new segments and must not alias the inputs.  A prefill batch
+ * (each request one run of tokens with one adapter) then has only segments whose rows
+ * are one run, which the prefill kernels move as 2-D tiles.  Same segment semantics as
+ * lf_group_tokens: any segmentation of the grouping gives the same products.
+ */
+int lf_split_runs(const int32_t* segment_indptr, const int32_t* segment_slots,
+                  const int32_t* token_indices, const int32_t* segment_count,
+                  int64_t num_tokens, int32_t chunk, int32_t* out_indptr,
+                  int32_t* out_slots, int32_t* out_count, void* stream);
+
+/*
  * Inverse of the grouping: routes[t] = the slot of the segment whose token_indices range
  * holds t, -1 for tokens in no segment.  Reads *segment_count on the device (segments
  * beyond it or beyond max_segments, index entries outside [0, num_indices) and
@@ -199,13 +214,14 @@ int lf_fused_shrink_expand(const void* x, int64_t x_stride, const void* a, const
 
 /*
  * Grouped (SGMV) shrink -> expand for prefill batches: the arguments and numerics of
- * lf_fused_shrink_expand, with segments of up to 128 tokens (group_tokens chunk 128).
- * Every segment runs on the tcgen05 tensor cores with TMEM accumulators (M = 128 tokens
- * per tile; shrink N = S*r rounded up to 16, K split in parts of 1024 whose FP32 partials
- * are added in order; expand N = 256 output columns, K = 64 zero-padded rank); a short
- * segment only leaves tile rows idle.  `workspace` holds at least
- * lf_sgmv_prefill_workspace_floats(...) floats, 16-byte aligned, zero-filled before its
- * first use (reused as for lf_fused_shrink_expand).  Replaces the prefill path of the
+ * lf_fused_shrink_expand, with segments of up to 128 tokens (group_tokens chunk 128;
+ * lf_split_runs for segments that are runs of tokens, whose x and y rows move as 2-D TMA
+ * tiles).  Every segment runs on the tcgen05 tensor cores with TMEM accumulators (M = 128
+ * tokens per tile; shrink N = S*r rounded up to 16, K split in up to 3 parts so that the
+ * segments fill the GPU in one wave; the expand adds the parts' FP32 partial z rows in
+ * part order, then N = 128 output columns, K = the rank bucket); a short segment only
+ * leaves tile rows idle.  `workspace` holds at least lf_sgmv_prefill_workspace_floats(...)
+ * floats, 16-byte aligned (no contents carry over between calls).  Replaces the prefill path of the
  * reference: the rank-aware SGMV shrink (src/loraforge/integrations/_sglang_rank_aware.py:
  * 14-171) and the chunked SGMV expand it pairs with (SGLang's
  * chunked_sgmv_lora_expand_forward, called at src/loraforge/integrations/

@@ -189,6 +189,160 @@ group_tokens_kernel(const int32_t* __restrict__ slots, int T, int num_slots, int
   }
 }
 
+// Block-wide scans of one int per thread (all kGroupThreads threads call them).
+__device__ int block_exclusive_sum(int v, int* wtmp, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, d);
+    if (lane >= d) x += y;
+  }
+  if (lane == 31) wtmp[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    const int w = wtmp[lane];
+    int xs = w;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, xs, d);
+      if (lane >= d) xs += y;
+    }
+    wtmp[lane] = xs - w;
+    if (lane == 31) *total = xs;
+  }
+  __syncthreads();
+  const int r = wtmp[warp] + x - v;
+  __syncthreads();
+  return r;
+}
+
+// Largest v of the threads before this one (-1 if none is larger).
+__device__ int block_exclusive_max(int v, int* wtmp) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, d);
+    if (lane >= d) x = max(x, y);
+  }
+  int ex = __shfl_up_sync(0xffffffffu, x, 1);
+  if (lane == 0) ex = -1;
+  if (lane == 31) wtmp[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int xs = wtmp[lane];
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, xs, d);
+      if (lane >= d) xs = max(xs, y);
+    }
+    int pex = __shfl_up_sync(0xffffffffu, xs, 1);
+    if (lane == 0) pex = -1;
+    wtmp[lane] = pex;
+  }
+  __syncthreads();
+  const int r = max(wtmp[warp], ex);
+  __syncthreads();
+  return r;
+}
+
+// Re-chunks a grouping so that no segment spans a gap in token order: inside each slot's
+// range of token_indices, a run is a maximal stretch of consecutive tokens, and each run
+// is cut into pieces of at most `chunk` tokens from its own start (chunk <= 0: one piece
+// per run).  token_indices is unchanged; the new segments go to out_*.  One CTA.
+//
+// First every position p gets a code in shared memory (coalesced, in parallel): bit 0 =
+// a run starts at p (a slot starts there, or token_indices[p] != token_indices[p-1] + 1),
+// bits 1.. = slot + 1 where a slot's range starts.  Then thread i walks a contiguous
+// stretch of positions three times (its last run / slot start, its segment count, then
+// its segments), with block scans carrying the run start and slot in from the left.
+// Without room for the codes (cached == 0) the walks read the tables in global memory.
+__global__ void __launch_bounds__(kGroupThreads)
+split_runs_kernel(const int32_t* __restrict__ in_indptr, const int32_t* __restrict__ in_slots,
+                  const int32_t* __restrict__ perm, const int32_t* __restrict__ in_count, int T,
+                  int chunk, int cached, int32_t* __restrict__ out_indptr,
+                  int32_t* __restrict__ out_slots, int32_t* __restrict__ out_count) {
+  extern __shared__ int code[];  // [T] when cached
+  __shared__ int wtmp[kGroupWarps];
+  __shared__ int total;
+  const int tid = threadIdx.x;
+  const int count = max(0, min(*in_count, T));
+  const int n = count > 0 ? max(0, min(in_indptr[count], T)) : 0;
+  if (cached) {
+    for (int p = tid; p < n; p += kGroupThreads)
+      code[p] = (p == 0 || perm[p] != perm[p - 1] + 1) ? 1 : 0;
+    __syncthreads();
+    for (int k = tid; k < count; k += kGroupThreads) {
+      const int slot = in_slots[k], at = in_indptr[k];
+      if ((k == 0 || in_slots[k - 1] != slot) && at >= 0 && at < n) code[at] = 1 | ((slot + 1) << 1);
+    }
+    __syncthreads();
+  }
+  const int per = (n + kGroupThreads - 1) / kGroupThreads;
+  const int b = min(n, tid * per), e = min(n, b + per);
+  // Global-memory walks: the input segment holding position b (last k with indptr <= b).
+  int k0 = 0;
+  if (!cached && b < e) {
+    int lo = 0, hi = count - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (in_indptr[mid] <= b) lo = mid;
+      else hi = mid - 1;
+    }
+    k0 = lo;
+  }
+  // visit(p, slot or -1 when unchanged, run_start)
+  auto walk = [&](auto&& visit) {
+    if (cached) {
+      for (int p = b; p < e; ++p) {
+        const int c = code[p];
+        visit(p, (c >> 1) - 1, (c & 1) != 0);
+      }
+      return;
+    }
+    int k = k0;
+    for (int p = b; p < e; ++p) {
+      while (k + 1 < count && in_indptr[k + 1] <= p) ++k;
+      const int slot = in_slots[k];
+      const bool slot_start = p == in_indptr[k] && (k == 0 || in_slots[k - 1] != slot);
+      visit(p, (slot_start || p == b) ? slot : -1, slot_start || p == 0 || perm[p] != perm[p - 1] + 1);
+    }
+  };
+  int last_run = -1, last_slot_pos = -1;
+  walk([&](int p, int slot, bool run_start) {
+    if (run_start) last_run = p;
+    if (slot >= 0) last_slot_pos = p;
+  });
+  const int carry = block_exclusive_max(last_run, wtmp);  // last run start before b
+  // The slot at position b: the slot start before it (cached codes), or the walk's own.
+  int cur = -1;
+  if (cached) {
+    const int from = block_exclusive_max(last_slot_pos, wtmp);
+    if (from >= 0) cur = (code[from] >> 1) - 1;
+  }
+  int start = carry, pieces = 0;
+  walk([&](int p, int, bool run_start) {
+    if (run_start) start = p;
+    if (run_start || (chunk > 0 && (p - start) % chunk == 0)) ++pieces;
+  });
+  int id = block_exclusive_sum(pieces, wtmp, &total);
+  start = carry;
+  walk([&](int p, int slot, bool run_start) {
+    if (slot >= 0) cur = slot;
+    if (run_start) start = p;
+    if (run_start || (chunk > 0 && (p - start) % chunk == 0)) {
+      out_indptr[id] = p;
+      out_slots[id] = cur;
+      ++id;
+    }
+  });
+  if (tid == 0) {
+    out_indptr[total] = n;
+    *out_count = total;
+  }
+}
+
 // routes[token_indices[i]] = segment_slots[s] for every i in segment s's range; one warp
 // per segment, grid-stride over segments.  Segments past *segment_count (or
 // max_segments), index entries outside [0, num_indices) and token positions outside
@@ -268,4 +422,28 @@ extern "C" int lf_group_tokens(const int32_t* slots, int64_t num_tokens, int32_t
       slots, T, num_slots, chunk, segment_indptr, segment_slots, token_indices,
       segment_count, cache, blocked);
   return check_launch("group_tokens");
+}
+
+extern "C" int lf_split_runs(const int32_t* segment_indptr, const int32_t* segment_slots,
+                             const int32_t* token_indices, const int32_t* segment_count,
+                             int64_t num_tokens, int32_t chunk, int32_t* out_indptr,
+                             int32_t* out_slots, int32_t* out_count, void* stream) {
+  using namespace lfb;
+  if (num_tokens < 0 || num_tokens >= (int64_t(1) << 31))
+    return fail(LF_E_INVALID, "split_runs: token count must fit signed int32");
+  if (!segment_indptr || !segment_count || !out_indptr || !out_count ||
+      (num_tokens && (!segment_slots || !token_indices || !out_slots)))
+    return fail(LF_E_INVALID, "split_runs: null buffer");
+  if (out_indptr == segment_indptr || out_slots == segment_slots || out_count == segment_count)
+    return fail(LF_E_INVALID, "split_runs: output tables must not alias the input tables");
+  // One int of shared memory per position when the batch fits (up to 51200 tokens).
+  const size_t limit = 200 * 1024;
+  const int cached = sizeof(int) * size_t(num_tokens) <= limit ? 1 : 0;
+  static int flags[64] = {};
+  if (int rc = ensure_smem(split_runs_kernel, int(limit), flags)) return rc;
+  split_runs_kernel<<<1, kGroupThreads, cached ? sizeof(int) * size_t(num_tokens) : 0,
+                      static_cast<cudaStream_t>(stream)>>>(segment_indptr, segment_slots, token_indices,
+                                                           segment_count, int(num_tokens), chunk, cached,
+                                                           out_indptr, out_slots, out_count);
+  return check_launch("split_runs");
 }

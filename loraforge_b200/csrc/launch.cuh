@@ -6,8 +6,10 @@
 namespace lfb {
 
 // Raise a kernel's dynamic shared-memory limit on the current device when `bytes`
-// exceeds what was configured there before.  `configured` holds one entry per device
-// (devices 0..63) for this kernel.
+// exceeds what was configured there before, and ask for the largest shared-memory
+// carveout: otherwise the driver may size the SM's split for one CTA of a kernel that
+// is meant to run two per SM (a function attribute of this process, not a device
+// setting).  `configured` holds one entry per device (devices 0..63) for this kernel.
 template <typename Kernel>
 inline int ensure_smem(Kernel kernel, int bytes, int* configured) {
   if (bytes <= 48 * 1024) return LF_OK;
@@ -16,7 +18,9 @@ inline int ensure_smem(Kernel kernel, int bytes, int* configured) {
   int& have = configured[device & 63];
   if (have >= bytes) return LF_OK;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) !=
-      cudaSuccess)
+          cudaSuccess ||
+      cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           cudaSharedmemCarveoutMaxShared) != cudaSuccess)
     return check_launch("cudaFuncSetAttribute");
   have = bytes;
   return LF_OK;

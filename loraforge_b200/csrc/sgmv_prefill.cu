@@ -14,7 +14,9 @@
 //   prefill_expand_kernel  y[seg, cols] += scale . z[seg] . B_g[cols]^T, one unit per
 //                          (segment, slice, 256-column block).  Two producer warps build the
 //                          segment's z tile (BF16 hi + lo of the FP32 z, scale folded in)
-//                          and stage the compact B rows of the block, zero-padded to 64;
+//                          and load the compact B rows of the block: TMA boxes in the
+//                          bucket's own swizzled layout for buckets 16 / 32 / 64 (K = the
+//                          bucket), else cp.async rows zero-padded to 64 (K = 64);
 //                          one thread issues M = 128, N = 256, K = 16 MMAs into one of two
 //                          TMEM accumulators; eight epilogue warps read the other one and
 //                          update the y rows (prefetched before the MMA completes).
@@ -51,11 +53,14 @@ constexpr int kMaxSlices = 4;
 constexpr int kMaxRank = 64;
 constexpr int kShrinkStages = 4;
 constexpr int kShrinkThreads = 160;          // 4 producer/epilogue warps + 1 MMA warp
-constexpr int kNT = 256;                     // expand columns per unit (UMMA N)
-constexpr int kBTileBytes = kNT * kRowBytes; // 32 KiB
-constexpr int kExpandThreads = 352;          // 8 epilogue, 2 producer, 1 MMA warp
-constexpr int kPartLen = 1024;               // K elements per shrink part
-constexpr int kBStages = 3;                  // expand B-tile ring
+constexpr int kNT = 128;                     // expand columns per unit (UMMA N)
+constexpr int kBTileBytes = kNT * kRowBytes; // 16 KiB
+constexpr int kYTileBytes = kTileM * kNT * 2;  // 32 KiB: two boxes of 128 rows x 64 columns
+constexpr int kExpandThreads = 384;          // 8 epilogue, producer, 2 z, MMA warps
+constexpr int kPartLen = 1024;               // K elements per shrink part, at least
+constexpr int kMaxParts = 3;                 // K parts of a call, at most
+constexpr int kEStages = 3;                  // expand B / y tile ring
+constexpr int kIdentBytes = 64 * kRowBytes;  // 64 x 64 BF16 identity, K-major, 128-B swizzle
 
 enum Numerics { kFp32 = 0, kReference = 1 };
 
@@ -75,17 +80,27 @@ struct PParams {
   const float* scales;
   const int32_t* slice_offsets;
   const int32_t* seg_count;
-  float* partial;     // [kparts][T][rpad]
-  float* zfinal;      // [T][rpad]: z of each token (row = permuted position)
-  int* counters;      // [T], zero between calls
+  float* partial;     // [kparts][T][rpad]: each K part's FP32 z rows (row = permuted position)
   int T, K, N, S, cap, num_slots, max_segments;
   int rpad;      // shrink UMMA N: S*min(cap, 64) rounded up to 16 (<= 256)
-  int kparts;    // K parts of kPartLen
+  int kparts;    // most K parts of a call (partial tables in the workspace)
+  int shrink_ctas;  // CTAs of the shrink grid
   int numerics;  // kFp32 or kReference
-  int pad;
-  CUtensorMap tmap_x;  // x as 2-D [T rows, K], boxes of 128 rows x 64 columns, 128-B swizzle
+  int y_mode;    // bit 0: y 16-byte aligned with stride a multiple of 8; bit 1: tmap_y valid
+  CUtensorMap tmap_x[5];  // x as 2-D [T rows, K], boxes of 64 columns x 128 / 64 / 32 / 16 / 8 rows
   CUtensorMap tmap_a;  // A as 2-D [slots*S*cap rows, K], boxes of rpad rows x 64 columns
+  // The compact B buffer as 2-D [rows, bucket] for bucket 16 / 32 / 64 ([0] / [1] / [2]),
+  // boxes of 128 ([.][0]) or 16 ([.][1]) rows, swizzled by the row's size (32 / 64 / 128
+  // bytes), so a box lands in the UMMA K-major layout of that bucket.  The row extent is
+  // nominal (kBRowsNominal): loads address only the rows of a slot's region, as the
+  // cp.async path does.
+  CUtensorMap tmap_b[3][2];
+  // y as 2-D [T rows, N], boxes of 64 columns x 128 / 64 / 32 / 16 / 8 rows, 128-B swizzle
+  // (the expand's tile loads of one run of tokens).
+  CUtensorMap tmap_y[5];
 };
+
+constexpr int64_t kBRowsNominal = (int64_t(1) << 31) - 1;
 
 struct PSeg {
   int ok, g, n, r, bucket, pos0;
@@ -101,6 +116,23 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 __device__ __forceinline__ int segment_total(const PParams& p) {
   const int n = *p.seg_count;
   return max(0, min(n, min(p.max_segments, p.T)));
+}
+
+// K split of the shrink: enough parts for the segments to fill the shrink grid in one
+// wave (at most kMaxParts, and parts of at least kPartLen), each a multiple of 64 long
+// and none empty.  The expand sums the parts' partial z rows in part order.
+struct KSplit {
+  int parts, len;
+};
+__device__ __forceinline__ KSplit k_split(const PParams& p, int nseg) {
+  const int want = max(1, min(p.kparts, p.shrink_ctas / max(1, nseg)));
+  const int len = ((p.K + want - 1) / want + 63) / 64 * 64;
+  return KSplit{(p.K + len - 1) / len, len};
+}
+
+// Box height (index into the x / y maps: 128, 64, 32, 16, 8 rows) covering n rows.
+__device__ __forceinline__ int box_rows_index(int n) {
+  return n > 64 ? 0 : n > 32 ? 1 : n > 16 ? 2 : n > 8 ? 3 : 4;
 }
 
 // Segment metadata; ok only for segments of 1..128 tokens whose slot, rank, bucket and
@@ -207,6 +239,22 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
          (uint64_t(1) << 46) | (uint64_t(2) << 61);
 }
 
+// The same for rows of 32, 64 or 128 bytes (bucket 16 / 32 / 64 BF16) swizzled by their
+// own size (layout type 6 / 4 / 2), 8-row groups 8 rows apart.
+__device__ __forceinline__ uint64_t swrow_desc(uint32_t saddr, int row_bytes) {
+  const uint64_t type = row_bytes == 128 ? 2 : row_bytes == 64 ? 4 : 6;
+  return uint64_t((saddr & 0x3FFFFu) >> 4) | (uint64_t(16 >> 4) << 16) |
+         (uint64_t((8 * row_bytes) >> 4) << 32) | (uint64_t(1) << 46) | (type << 61);
+}
+
+// Byte offset of 16-byte chunk c of row r in a tile of row_bytes-byte rows swizzled by
+// row_bytes (address bits 4.. XOR bits 7..; tile base aligned to 8 rows).
+__device__ __forceinline__ uint32_t swz_rows(int r, int c, int row_bytes) {
+  const uint32_t off = uint32_t(r) * uint32_t(row_bytes) + (uint32_t(c) << 4);
+  const uint32_t mask = uint32_t(row_bytes >> 4) - 1u;
+  return off ^ (((off >> 7) & mask) << 4);
+}
+
 // Instruction descriptor, kind::f16: BF16 A and B (K-major), FP32 D, M x N.
 __host__ __device__ constexpr uint32_t idesc_bf16(int m, int n) {
   return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
@@ -264,7 +312,9 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
 // row with cp.async.  The stage's "full" barrier takes 129 arrivals: thread 0's
 // expect-tx arrive for the TMA bytes and one arrive per producer thread once its own
 // copies (if any) have landed and been made visible to the tensor cores' proxy.
-__global__ void __launch_bounds__(kShrinkThreads, 1) prefill_shrink_kernel(const __grid_constant__ PParams p) {
+// Two CTAs per SM: their ten warps put three on some SM sub-partition (16 K registers
+// each), so a thread may hold at most 168 registers.
+__global__ void __maxnreg__(168) prefill_shrink_kernel(const __grid_constant__ PParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -275,8 +325,7 @@ __global__ void __launch_bounds__(kShrinkThreads, 1) prefill_shrink_kernel(const
   uint64_t* acc_empty = acc_full + 1;
   uint64_t* fin = acc_empty + 1;  // the MMA thread's last commit (all MMAs retired)
   uint32_t* tslot = reinterpret_cast<uint32_t*>(fin + 1);
-  int* flag = reinterpret_cast<int*>(tslot + 1);
-  volatile int* abort = reinterpret_cast<volatile int*>(flag + 1);
+  volatile int* abort = reinterpret_cast<volatile int*>(tslot + 2);
   const uint32_t tcols = p.rpad <= 32 ? 32u : (p.rpad <= 64 ? 64u : (p.rpad <= 128 ? 128u : 256u));
 
   if (tid == 0) {
@@ -298,19 +347,20 @@ __global__ void __launch_bounds__(kShrinkThreads, 1) prefill_shrink_kernel(const
   pdl_wait();
   pdl_launch_dependents();  // only after this CTA holds its TMEM columns
 
-  const int total = segment_total(p) * p.kparts;
+  const KSplit ks = k_split(p, segment_total(p));
+  const int total = segment_total(p) * ks.parts;
   if (warp < 4) {
     // ------------------------------------------- producers, then epilogue, per unit
     const int row = tid;  // tile row == TMEM lane
     int sidx = 0;         // stage uses so far (ring position)
     int units = 0;
     for (int u = blockIdx.x; u < total; u += gridDim.x) {
-      const int seg = u / p.kparts, kp = u - seg * p.kparts;
+      const int seg = u / ks.parts, kp = u - seg * ks.parts;
       const PSeg si = prefill_segment(p, seg);
       if (!si.ok) continue;
       if (any128(*abort)) break;  // an expired wait: stop together (barriers below)
-      const int k0 = kp * kPartLen;
-      const int kend = min(p.K, k0 + kPartLen);
+      const int k0 = kp * ks.len;
+      const int kend = min(p.K, k0 + ks.len);
       const int nsteps = (kend - k0 + 63) / 64;
       int tok = -1;
       if (row < si.n) {
@@ -330,9 +380,12 @@ __global__ void __launch_bounds__(kShrinkThreads, 1) prefill_shrink_kernel(const
         const uint32_t st = smem_u32(smem + stage * SB);
         const int kk = k0 + s * 64;
         if (tid == 0) {
-          mbar_arrive_expect_tx(&full[stage], uint32_t(p.rpad * kRowBytes + (run ? kXTileBytes : 0)));
+          // x: a box of the smallest height covering the segment's rows (the rows past it
+          // feed accumulator rows that are never stored).
+          const int h = box_rows_index(si.n);
+          mbar_arrive_expect_tx(&full[stage], uint32_t(p.rpad * kRowBytes + (run ? (kTileM >> h) * kRowBytes : 0)));
           tma_load_2d(st + kXTileBytes, &p.tmap_a, kk, arow0, &full[stage]);
-          if (run) tma_load_2d(st, &p.tmap_x, kk, first, &full[stage]);
+          if (run) tma_load_2d(st, &p.tmap_x[h], kk, first, &full[stage]);
         }
         if (run) {
           mbar_arrive(&full[stage]);
@@ -385,57 +438,23 @@ __global__ void __launch_bounds__(kShrinkThreads, 1) prefill_shrink_kernel(const
       }
       tc_fence_before();
       mbar_arrive(acc_empty);
-      // The CTA that completes the segment's count adds the parts in order into z.
-      __threadfence();
-      named_barrier(1, kTileM);
-      if (tid == 0) {
-        const int old = atomicAdd(&p.counters[seg], 1);
-        *flag = old == p.kparts - 1 ? 1 : 0;
-      }
-      named_barrier(1, kTileM);
-      if (*flag) {
-        __threadfence();
-        if (row < si.n) {
-          const int64_t pos = si.pos0 + row;
-          for (int jb = 0; jb < p.rpad; jb += 64) {
-            const int nv = min(64, p.rpad - jb) / 4;  // float4s in this block (rpad % 16 == 0)
-            float4 acc[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int q = 0; q < p.kparts; ++q) {
-              const float4* src = reinterpret_cast<const float4*>(p.partial + (int64_t(q) * p.T + pos) * p.rpad + jb);
-              float4 v[16];
-#pragma unroll
-              for (int i = 0; i < 16; ++i) v[i] = i < nv ? __ldcg(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                acc[i].x += v[i].x;
-                acc[i].y += v[i].y;
-                acc[i].z += v[i].z;
-                acc[i].w += v[i].w;
-              }
-            }
-            float4* dst = reinterpret_cast<float4*>(p.zfinal + pos * p.rpad + jb);
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-              if (i < nv) dst[i] = acc[i];
-          }
-        }
-        if (tid == 0) p.counters[seg] = 0;
-      }
-      named_barrier(1, kTileM);  // *flag is rewritten by the next unit
     }
+    // No box may still be landing when the CTA exits (the normal path has consumed every
+    // stage already; after an expired wait this waits, bounded, for the last ones).
+    if (tid == 0)
+      for (int j = max(0, sidx - kShrinkStages); j < sidx; ++j)
+        mbar_wait(&full[j % kShrinkStages], uint32_t(j / kShrinkStages) & 1u);
   } else if (warp == 4 && lane == 0) {
     // ------------------------------------------------------------ MMA thread
     const uint32_t idesc = idesc_bf16(kTileM, p.rpad);
     int sidx = 0, units = 0;
     for (int u = blockIdx.x; u < total; u += gridDim.x) {
-      const int seg = u / p.kparts, kp = u - seg * p.kparts;
+      const int seg = u / ks.parts, kp = u - seg * ks.parts;
       const PSeg si = prefill_segment(p, seg);
       if (!si.ok) continue;
       if (*abort) break;
-      const int k0 = kp * kPartLen;
-      const int nsteps = (min(p.K, k0 + kPartLen) - k0 + 63) / 64;
+      const int k0 = kp * ks.len;
+      const int nsteps = (min(p.K, k0 + ks.len) - k0 + 63) / 64;
       if (units > 0) wait_or_abort(acc_empty, uint32_t(units - 1) & 1u, abort);
       tc_fence_after();
       for (int s = 0; s < nsteps; ++s, ++sidx) {
@@ -465,7 +484,7 @@ __global__ void __launch_bounds__(kShrinkThreads, 1) prefill_shrink_kernel(const
 
 // ====================================================================== expand
 // Unit u of a CTA: segment u / nb, block u % nb, where a segment's nb blocks cover every
-// slice in 256-column pieces (no block straddles two slices).
+// slice in 128-column pieces (no block straddles two slices).
 struct Block {
   int slice, c0, width;  // slice, first column inside the slice, slice width
 };
@@ -487,16 +506,113 @@ __device__ __forceinline__ Block block_of(const int* offs, int S, int b) {
   return k;
 }
 
+// Bucket of a segment's B rows when they are loaded by TMA boxes (16, 32 or 64: rows of
+// 32 / 64 / 128 bytes, B offset a whole number of rows, row coordinates inside int32),
+// else 0: rows zero-padded to 64 elements and staged with cp.async.
+__device__ __forceinline__ int b_box_bucket(const PSeg& s, const PParams& p) {
+  const bool sized = s.bucket == 16 || s.bucket == 32 || s.bucket == 64;
+  return sized && s.boff % s.bucket == 0 && s.boff / s.bucket + p.N <= kBRowsNominal ? s.bucket : 0;
+}
+
+// How a unit's y rows come in.  kYTma: the segment's tokens are one run (token_indices
+// is ascending inside a slot's group, so equal spans mean a run) and y has tensor maps:
+// TMA boxes.  kYGather: rows gathered through token_indices, or no tensor maps:
+// coalesced cp.async.  Both stage the tile in shared memory, from where the epilogue
+// stores it back coalesced, and need 16-byte aligned rows and a block that starts on a
+// multiple of 8 columns; kYDirect (otherwise): the epilogue threads read and write their
+// rows in global memory.
+enum YMode { kYDirect = 0, kYGather = 1, kYTma = 2 };
+struct YUnit {
+  int mode, tok0;  // tok0: first token of a run, else -1
+};
+__device__ __forceinline__ YUnit y_unit(const PParams& p, int run, int gcol0) {
+  YUnit r{kYDirect, -1};
+  if (!(p.y_mode & 1) || (gcol0 & 7)) return r;
+  r.mode = run >= 0 && (p.y_mode & 2) ? kYTma : kYGather;
+  r.tok0 = run;
+  return r;
+}
+
+// Segment metadata of a role's current unit, looked up again only when the segment
+// changes (a CTA's units are consecutive blocks, mostly of one segment).  run: the first
+// token when the segment's rows are one run of tokens, else -1.
+struct SegCache {
+  int seg = -1, run = -1;
+  int kb = 0, brow = 0;  // b_box_bucket and the slot's first B row in bucket-wide rows
+  PSeg si{};
+  __device__ __forceinline__ const PSeg& get(const PParams& p, int s) {
+    if (s != seg) {
+      seg = s;
+      si = prefill_segment(p, s);
+      run = -1;
+      kb = brow = 0;
+      if (si.ok) {
+        const int first = p.perm[si.pos0], last = p.perm[si.pos0 + si.n - 1];
+        if (first >= 0 && last < p.T && last - first == si.n - 1) run = first;
+        kb = b_box_bucket(si, p);
+        if (kb) brow = int(si.boff / kb);
+      }
+    }
+    return si;
+  }
+};
+
+// Token of row m of a segment (-1 when token_indices holds an invalid entry).
+__device__ __forceinline__ int row_token(const PParams& p, const PSeg& si, const YUnit& yu, int m) {
+  if (yu.tok0 >= 0) return yu.tok0 + m;
+  const int t = p.perm[si.pos0 + m];
+  return t >= 0 && t < p.T ? t : -1;
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ uint4 lds16(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
+// y + delta for 8 columns: old y (BF16 x 8) and 8 FP32 accumulator values.
+template <int MODE>
+__device__ __forceinline__ uint4 y_update(uint4 o, const uint32_t* d, float scale) {
+  const uint32_t ow[4] = {o.x, o.y, o.z, o.w};
+  uint32_t nw[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float d0 = __uint_as_float(d[2 * e]), d1 = __uint_as_float(d[2 * e + 1]);
+    const float y0 = __uint_as_float(ow[e] << 16), y1 = __uint_as_float(ow[e] & 0xffff0000u);
+    const float v0 = MODE == kFp32 ? y0 + d0 : y0 + round_through_bf16(d0 * scale);
+    const float v1 = MODE == kFp32 ? y1 + d1 : y1 + round_through_bf16(d1 * scale);
+    nw[e] = cvt_bf16x2(v0, v1);
+  }
+  return make_uint4(nw[0], nw[1], nw[2], nw[3]);
+}
+
+// Warp roles: 0-7 epilogue (TMEM lane quarter = warp & 3, 64-column half = warp >> 2;
+// they also store the updated y tile), 8 producer (B and y tiles), 9-10 z tiles, 11 MMA
+// thread (and the TMEM allocation).  Rings: B / y tiles in kEStages stages, z tiles and
+// TMEM accumulators (128 columns each) in 2.
 template <int MODE>
 __global__ void __launch_bounds__(kExpandThreads, 1) prefill_expand_kernel(const __grid_constant__ PParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  uint8_t* btile = smem;                           // kBStages x 32 KiB
-  uint8_t* ztile = smem + kBStages * kBTileBytes;  // 2 buffers x (hi, lo) x 16 KiB
-  uint64_t* b_full = reinterpret_cast<uint64_t*>(ztile + 4 * kXTileBytes);
-  uint64_t* b_empty = b_full + kBStages;
-  uint64_t* z_full = b_empty + kBStages;
+  uint8_t* ytile = smem;                               // kEStages x 32 KiB (two 64-column boxes)
+  uint8_t* btile = ytile + kEStages * kYTileBytes;     // kEStages x 16 KiB
+  uint8_t* ztile = btile + kEStages * kBTileBytes;     // 2 buffers x (hi, lo) x 16 KiB
+  uint8_t* ident = ztile + 4 * kXTileBytes;  // 64 x 64 BF16 identity (FP32 numerics: adds y)
+  uint64_t* b_full = reinterpret_cast<uint64_t*>(ident + kIdentBytes);
+  uint64_t* b_empty = b_full + kEStages;
+  uint64_t* y_full = b_empty + kEStages;
+  uint64_t* y_done = y_full + kEStages;   // every epilogue thread has updated its rows
+  uint64_t* y_empty = y_done + kEStages;  // ... and stored its share of the tile
+  uint64_t* z_full = y_empty + kEStages;
   uint64_t* z_empty = z_full + 2;
   uint64_t* t_full = z_empty + 2;
   uint64_t* t_empty = t_full + 2;
@@ -504,15 +620,19 @@ __global__ void __launch_bounds__(kExpandThreads, 1) prefill_expand_kernel(const
   uint32_t* tslot = reinterpret_cast<uint32_t*>(fin + 1);
   int* offs = reinterpret_cast<int*>(tslot + 4);
   volatile int* abort = reinterpret_cast<volatile int*>(offs + kMaxSlices + 2);
-  constexpr int kEpi = 256, kProd = 64;
+  int* tokrow = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(b_full) + 320);  // kEStages x 128 row tokens
+  constexpr int kEpi = 256, kZ = 64;
 
   if (tid == 0) {
-    for (int i = 0; i < kBStages; ++i) {
-      mbar_init(&b_full[i], kProd);
+    for (int i = 0; i < kEStages; ++i) {
+      mbar_init(&b_full[i], 32);  // the producer warp (lane 0 also expects the boxes' bytes)
       mbar_init(&b_empty[i], 1);
+      mbar_init(&y_full[i], 32);  // the producer warp (lane 0 also expects the boxes' bytes)
+      mbar_init(&y_done[i], kEpi);
+      mbar_init(&y_empty[i], kEpi);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&z_full[i], kProd);
+      mbar_init(&z_full[i], kZ);
       mbar_init(&z_empty[i], 1);
       mbar_init(&t_full[i], 1);
       mbar_init(&t_empty[i], kEpi);
@@ -522,7 +642,18 @@ __global__ void __launch_bounds__(kExpandThreads, 1) prefill_expand_kernel(const
     *abort = 0;
   }
   if (tid <= p.S) offs[tid] = p.slice_offsets[tid];
-  if (warp == 10) tc_alloc(tslot, 512);
+  if (MODE == kFp32) {
+    // Row n holds 1.0 at column n: y box j (128 tokens x 64 columns) times it adds y to
+    // the accumulator's columns 64j..64j+63.
+    for (int i = tid; i < 64 * 8; i += kExpandThreads) {
+      const int r = i >> 3, c = i & 7;
+      uint32_t w[4] = {0u, 0u, 0u, 0u};
+      if ((r >> 3) == c) w[(r & 7) >> 1] = 0x3F80u << (16 * (r & 1));
+      sts16(smem_u32(ident) + swz(r, c), make_uint4(w[0], w[1], w[2], w[3]));
+    }
+    fence_async_smem();
+  }
+  if (warp == 11) tc_alloc(tslot, 2 * kNT);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -530,127 +661,241 @@ __global__ void __launch_bounds__(kExpandThreads, 1) prefill_expand_kernel(const
   pdl_launch_dependents();  // only after this CTA holds its TMEM columns
 
   const int nseg = segment_total(p);
+  const KSplit ks = k_split(p, nseg);  // the shrink's partial z tables
   int nb = 0;
   for (int s = 0; s < p.S; ++s) nb += (offs[s + 1] - offs[s] + kNT - 1) / kNT;
   const int total = nseg * nb;
   const int per = (total + int(gridDim.x) - 1) / int(gridDim.x);
   const int u0 = min(total, int(blockIdx.x) * per), u1 = min(total, u0 + per);
 
-  if (warp == 8 || warp == 9) {
-    // ------------------------------------------------------------ producers
-    const int pt = tid - kEpi;
-    bool waited = false;
-    int bidx = 0, zcount = 0, key = -1, pend = -1;
+  if (warp == 8) {
+    // ------------------------------------------------------------ producer
+    // y tile: boxes of 128 token rows x 64 columns (rows past the segment and columns past
+    // the slice are read but never stored; past the tensor they read as zero).  B rows:
+    // buckets 16 / 32 / 64 in TMA boxes of 128 and 16 rows in the bucket's own swizzled
+    // layout, cp.async for the last rows under 16; rows past the slice are left as they
+    // are (they only feed accumulator columns nobody stores).  Other buckets and offsets:
+    // every row zero-padded to 64 elements through cp.async.
+    int it = 0, pend = -1;
+    bool pend_b = false, pend_y = false;
+    SegCache sc;
     for (int u = u0; u < u1; ++u) {
       const int seg = u / nb;
       const Block blk = block_of(offs, p.S, u - seg * nb);
-      const PSeg si = prefill_segment(p, seg);
+      const PSeg& si = sc.get(p, seg);
       if (!si.ok || blk.slice < 0) continue;
       if (*abort) break;
-      // B rows of the block, zero-padded to 64 elements (3-stage ring).
-      const int bs = bidx % kBStages;
-      wait_or_abort(&b_empty[bs], (uint32_t(bidx / kBStages) & 1u) ^ 1u, abort);
-      ++bidx;
-      const uint32_t bt = smem_u32(btile + bs * kBTileBytes);
+      const int s = it % kEStages;
+      const uint32_t ph = (uint32_t(it / kEStages) & 1u) ^ 1u;
+      if (!wait_or_abort(&b_empty[s], ph, abort) || !wait_or_abort(&y_empty[s], ph, abort)) break;
+      ++it;
       const int gcol0 = offs[blk.slice] + blk.c0;
-      for (int i = pt; i < kNT * 8; i += kProd) {
-        const int r = i >> 3, c = i & 7, k = 8 * c;
-        const bool live = blk.c0 + r < blk.width && k < si.bucket;
-        const uint16_t* src = p.b + si.boff + int64_t(gcol0 + r) * si.bucket + k;
-        if (si.bucket >= 8) {
-          cp16(bt + swz(r, c), live ? static_cast<const void*>(src) : p.b, live ? 16u : 0u);
-        } else {
-          uint32_t w[4] = {0u, 0u, 0u, 0u};
-          if (live)
-            for (int e = 0; e < si.bucket; ++e) w[e >> 1] |= uint32_t(src[e]) << (16 * (e & 1));
-          sts16(bt + swz(r, c), make_uint4(w[0], w[1], w[2], w[3]));
+      const int cols = min(kNT, blk.width - blk.c0);
+      const YUnit yu = y_unit(p, sc.run, gcol0);
+      const uint32_t yt = smem_u32(ytile + s * kYTileBytes);
+      int* trow = tokrow + s * kTileM;
+      if (yu.mode != kYDirect) {
+        // The rows' tokens, for the copies below and the epilogue's stores (all four
+        // loads of a lane are issued before any is used).
+        int tk[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) tk[q] = lane + 32 * q < si.n ? row_token(p, si, yu, lane + 32 * q) : -1;
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (lane + 32 * q < si.n) trow[lane + 32 * q] = tk[q];
+        __syncwarp();
+      }
+      if (yu.mode == kYTma && lane == 0) {
+        // Boxes of the smallest height of 128 / 64 / 32 / 16 / 8 rows that covers the
+        // segment; expected bytes before any box can complete.
+        const int h = box_rows_index(si.n);
+        const int nbox = (cols + 63) >> 6;
+        mbar_expect_tx(&y_full[s], uint32_t(nbox * (kTileM >> h) * kRowBytes));
+        for (int j = 0; j < nbox; ++j)
+          tma_load_2d(yt + uint32_t(j * kXTileBytes), &p.tmap_y[h], gcol0 + 64 * j, yu.tok0, &y_full[s]);
+      }
+      const bool ycp = yu.mode == kYGather;  // the y tile has cp.async copies
+      if (ycp) {
+        // Row m, 16-byte chunk cc of the block's 16 (box cc / 8): four rows per warp step.
+        for (int i = lane; i < si.n * 16; i += 32) {
+          const int m = i >> 4, cc = i & 15, col = 8 * cc;
+          const int tok = trow[m];
+          if (col >= cols || tok < 0) continue;
+          const int left = p.N - (gcol0 + col);  // columns of y's row from here (> 0)
+          cp16(yt + uint32_t((cc >> 3) * kXTileBytes) + swz(m, cc & 7), p.y + int64_t(tok) * p.y_stride + gcol0 + col,
+               left >= 8 ? 16u : uint32_t(2 * left));
+        }
+      }
+      const uint32_t bt = smem_u32(btile + s * kBTileBytes);
+      const int kb = sc.kb;
+      bool staged = true;  // the B tile has cp.async copies
+      if (kb) {
+        const int rb = 2 * kb, cpr = rb >> 4;
+        const int n128 = cols >> 7, n16 = (cols & 127) >> 4, boxed = cols & ~15;
+        const int row0 = sc.brow + gcol0;
+        const int m = kb == 16 ? 0 : kb == 32 ? 1 : 2;
+        if (lane == 0 && boxed > 0) {
+          // Expected bytes before any box can complete; this lane arrives afterwards.
+          mbar_expect_tx(&b_full[s], uint32_t(boxed * rb));
+          for (int i = 0; i < n128; ++i)
+            tma_load_2d(bt + uint32_t(128 * i * rb), &p.tmap_b[m][0], 0, row0 + 128 * i, &b_full[s]);
+          for (int i = 0; i < n16; ++i) {
+            const int r = 128 * n128 + 16 * i;
+            tma_load_2d(bt + uint32_t(r * rb), &p.tmap_b[m][1], 0, row0 + r, &b_full[s]);
+          }
+        }
+        staged = boxed < cols;
+        for (int i = lane; i < (cols - boxed) * cpr; i += 32) {
+          const int r = boxed + i / cpr, c = i % cpr;
+          cp16(bt + swz_rows(r, c, rb), p.b + si.boff + int64_t(gcol0 + r) * kb + 8 * c, 16u);
+        }
+      } else {
+        for (int i = lane; i < kNT * 8; i += 32) {
+          const int r = i >> 3, c = i & 7, k = 8 * c;
+          const bool live = r < cols && k < si.bucket;
+          const uint16_t* src = p.b + si.boff + int64_t(gcol0 + r) * si.bucket + k;
+          if (si.bucket >= 8) {
+            cp16(bt + swz(r, c), live ? static_cast<const void*>(src) : p.b, live ? 16u : 0u);
+          } else {
+            uint32_t w[4] = {0u, 0u, 0u, 0u};
+            if (live)
+              for (int e = 0; e < si.bucket; ++e) w[e >> 1] |= uint32_t(src[e]) << (16 * (e & 1));
+            sts16(bt + swz(r, c), make_uint4(w[0], w[1], w[2], w[3]));
+          }
         }
       }
       cp_commit();
-      // The previous block is handed over once its copies have landed (one block of
-      // lag keeps two in flight).
+      // A tile with cp.async copies is handed over once they have landed (one unit of lag
+      // keeps two in flight); a tile of boxes alone at once, since its barrier phase also
+      // waits for the boxes' bytes.
       if (pend >= 0) {
         cp_wait<1>();
         fence_async_smem();
-        mbar_arrive(&b_full[pend]);
-      }
-      pend = bs;
-      // z tile of (segment, slice): the shrink's BF16 hi / lo rows, swizzled.
-      const int k2 = seg * kMaxSlices + blk.slice;
-      if (k2 != key) {
-        key = k2;
-        if (!waited) {
-          pdl_wait();  // the z rows are written by the preceding shrink grid
-          waited = true;
-        }
-        const int zb = zcount & 1;
-        wait_or_abort(&z_empty[zb], (uint32_t(zcount >> 1) & 1u) ^ 1u, abort);
-        ++zcount;
-        // BF16 hi + lo of scale * z (FP32 numerics) or bf16(z) (reference), zero beyond
-        // min(rank, bucket) and past the segment's rows; 8 elements per thread step.
-        const uint32_t zh = smem_u32(ztile + zb * 2 * kXTileBytes), zl = zh + kXTileBytes;
-        const int live = min(si.r, si.bucket);
-        const float mul = MODE == kFp32 ? si.scale : 1.f;
-        const int col0 = blk.slice * si.r;
-        const bool vec = (col0 & 3) == 0;
-        // Four items per pass: all their loads are issued before any conversion.
-        for (int i0 = pt; i0 < kTileM * 8; i0 += 4 * kProd) {
-          float v[4][8];
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int i = i0 + q * kProd, m = i >> 3, c = i & 7;
-            const float* src = p.zfinal + int64_t(si.pos0 + m) * p.rpad + col0 + 8 * c;
-            if (i < kTileM * 8 && m < si.n && vec && 8 * c + 8 <= live) {
-              const float4 a0 = __ldcg(reinterpret_cast<const float4*>(src));
-              const float4 a1 = __ldcg(reinterpret_cast<const float4*>(src) + 1);
-              v[q][0] = a0.x; v[q][1] = a0.y; v[q][2] = a0.z; v[q][3] = a0.w;
-              v[q][4] = a1.x; v[q][5] = a1.y; v[q][6] = a1.z; v[q][7] = a1.w;
-            } else {
-#pragma unroll
-              for (int e = 0; e < 8; ++e)
-                v[q][e] = (i < kTileM * 8 && m < si.n && 8 * c + e < live) ? __ldcg(src + e) : 0.f;
-            }
-          }
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int i = i0 + q * kProd, m = i >> 3, c = i & 7;
-            if (i >= kTileM * 8) break;
-            uint32_t hw[4], lw[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float v0 = mul * v[q][2 * e], v1 = mul * v[q][2 * e + 1];
-              hw[e] = cvt_bf16x2(v0, v1);
-              const float h0 = __uint_as_float(hw[e] << 16), h1 = __uint_as_float(hw[e] & 0xffff0000u);
-              lw[e] = cvt_bf16x2(v0 - h0, v1 - h1);
-            }
-            sts16(zh + swz(m, c), make_uint4(hw[0], hw[1], hw[2], hw[3]));
-            if (MODE == kFp32) sts16(zl + swz(m, c), make_uint4(lw[0], lw[1], lw[2], lw[3]));
-          }
-        }
-        cp_commit();
-        cp_wait<0>();
-        fence_async_smem();
-        mbar_arrive(&b_full[pend]);
+        if (pend_b) mbar_arrive(&b_full[pend]);
+        if (pend_y) mbar_arrive(&y_full[pend]);
         pend = -1;
-        mbar_arrive(&z_full[zb]);
+      }
+      if (!staged) mbar_arrive(&b_full[s]);
+      if (!ycp) mbar_arrive(&y_full[s]);
+      if (staged || ycp) {
+        pend = s;
+        pend_b = staged;
+        pend_y = ycp;
       }
     }
     if (pend >= 0) {
       cp_wait<0>();
       fence_async_smem();
-      mbar_arrive(&b_full[pend]);
+      if (pend_b) mbar_arrive(&b_full[pend]);
+      if (pend_y) mbar_arrive(&y_full[pend]);
+    }
+    // No box may still be landing when the CTA exits (the normal path has consumed every
+    // stage already; after an expired wait this waits, bounded, for the last ones).
+    if (lane == 0)
+      for (int j = max(0, it - kEStages); j < it; ++j) {
+        mbar_wait(&b_full[j % kEStages], uint32_t(j / kEStages) & 1u);
+        mbar_wait(&y_full[j % kEStages], uint32_t(j / kEStages) & 1u);
+      }
+  } else if (warp == 9 || warp == 10) {
+    // ------------------------------------------------------------ z tiles
+    const int zt = tid - 9 * 32;
+    bool waited = false;
+    int zcount = 0, key = -1;
+    SegCache sc;
+    for (int u = u0; u < u1; ++u) {
+      const int seg = u / nb;
+      const Block blk = block_of(offs, p.S, u - seg * nb);
+      const PSeg& si = sc.get(p, seg);
+      if (!si.ok || blk.slice < 0) continue;
+      if (*abort) break;
+      const int k2 = seg * kMaxSlices + blk.slice;
+      if (k2 == key) continue;
+      key = k2;
+      if (!waited) {
+        pdl_wait();  // the z rows are written by the preceding shrink grid
+        waited = true;
+      }
+      const int zb = zcount & 1;
+      wait_or_abort(&z_empty[zb], (uint32_t(zcount >> 1) & 1u) ^ 1u, abort);
+      ++zcount;
+      // z = the shrink's partial rows summed in part order (from 0), then BF16 hi + lo of
+      // scale * z (FP32 numerics) or bf16(z) (reference), zero beyond min(rank, bucket) and
+      // past the segment's rows; 8 elements per item, four items per pass with every
+      // part's loads of all four issued before any sum.
+      const uint32_t zh = smem_u32(ztile + zb * 2 * kXTileBytes), zl = zh + kXTileBytes;
+      const int live = min(si.r, si.bucket);
+      const float mul = MODE == kFp32 ? si.scale : 1.f;
+      const int col0 = blk.slice * si.r;
+      const bool vec = (col0 & 3) == 0;
+      const int64_t part_stride = int64_t(p.T) * p.rpad;
+      constexpr int kItems = 4;
+      for (int i0 = zt; i0 < kTileM * 8; i0 += kItems * kZ) {
+        float v[kItems][8];
+        float4 ld[kItems][kMaxParts][2];
+#pragma unroll
+        for (int q = 0; q < kItems; ++q) {
+          const int i = i0 + q * kZ, m = i >> 3, c = i & 7;
+          const float* src = p.partial + int64_t(si.pos0 + m) * p.rpad + col0 + 8 * c;
+          const bool full8 = i < kTileM * 8 && m < si.n && vec && 8 * c + 8 <= live;
+#pragma unroll
+          for (int pp = 0; pp < kMaxParts; ++pp) {
+            if (full8 && pp < ks.parts) {
+              ld[q][pp][0] = __ldcg(reinterpret_cast<const float4*>(src + pp * part_stride));
+              ld[q][pp][1] = __ldcg(reinterpret_cast<const float4*>(src + pp * part_stride) + 1);
+            }
+          }
+        }
+#pragma unroll
+        for (int q = 0; q < kItems; ++q) {
+          const int i = i0 + q * kZ, m = i >> 3, c = i & 7;
+          const float* src = p.partial + int64_t(si.pos0 + m) * p.rpad + col0 + 8 * c;
+          const bool full8 = i < kTileM * 8 && m < si.n && vec && 8 * c + 8 <= live;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[q][e] = 0.f;
+          if (full8) {
+#pragma unroll
+            for (int pp = 0; pp < kMaxParts; ++pp) {
+              if (pp < ks.parts) {
+                v[q][0] += ld[q][pp][0].x; v[q][1] += ld[q][pp][0].y; v[q][2] += ld[q][pp][0].z; v[q][3] += ld[q][pp][0].w;
+                v[q][4] += ld[q][pp][1].x; v[q][5] += ld[q][pp][1].y; v[q][6] += ld[q][pp][1].z; v[q][7] += ld[q][pp][1].w;
+              }
+            }
+          } else if (i < kTileM * 8 && m < si.n) {
+            for (int e = 0; e < 8 && 8 * c + e < live; ++e)
+              for (int pp = 0; pp < ks.parts; ++pp) v[q][e] += __ldcg(src + pp * part_stride + e);
+          }
+        }
+#pragma unroll
+        for (int q = 0; q < kItems; ++q) {
+          const int i = i0 + q * kZ, m = i >> 3, c = i & 7;
+          if (i >= kTileM * 8) break;
+          uint32_t hw[4], lw[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float v0 = mul * v[q][2 * e], v1 = mul * v[q][2 * e + 1];
+            hw[e] = cvt_bf16x2(v0, v1);
+            const float h0 = __uint_as_float(hw[e] << 16), h1 = __uint_as_float(hw[e] & 0xffff0000u);
+            lw[e] = cvt_bf16x2(v0 - h0, v1 - h1);
+          }
+          sts16(zh + swz(m, c), make_uint4(hw[0], hw[1], hw[2], hw[3]));
+          if (MODE == kFp32) sts16(zl + swz(m, c), make_uint4(lw[0], lw[1], lw[2], lw[3]));
+        }
+      }
+      fence_async_smem();
+      mbar_arrive(&z_full[zb]);
     }
     // Every CTA waits for the shrink grid, so this grid's completion implies the shrink's.
     if (!waited) pdl_wait();
-  } else if (warp == 10) {
+  } else if (warp == 11) {
     // ------------------------------------------------------------ MMA thread
     if (lane == 0) {
-      const uint32_t idesc = idesc_bf16(kTileM, kNT);
-      int bidx = 0, zcount = 0, tcount = 0, key = -1, zb = 0;
+      const uint32_t idesc = idesc_bf16(kTileM, kNT), idesc64 = idesc_bf16(kTileM, 64);
+      int it = 0, zcount = 0, tcount = 0, key = -1, zb = 0;
+      SegCache sc;
       for (int u = u0; u < u1; ++u) {
         const int seg = u / nb;
         const Block blk = block_of(offs, p.S, u - seg * nb);
-        const PSeg si = prefill_segment(p, seg);
+        const PSeg& si = sc.get(p, seg);
         if (!si.ok || blk.slice < 0) continue;
         if (*abort) break;
         const int k2 = seg * kMaxSlices + blk.slice;
@@ -661,9 +906,13 @@ __global__ void __launch_bounds__(kExpandThreads, 1) prefill_expand_kernel(const
           wait_or_abort(&z_full[zb], uint32_t(zcount >> 1) & 1u, abort);
           ++zcount;
         }
-        const int bs = bidx % kBStages;
-        wait_or_abort(&b_full[bs], uint32_t(bidx / kBStages) & 1u, abort);
-        ++bidx;
+        const int s = it % kEStages;
+        const uint32_t sph = uint32_t(it / kEStages) & 1u;
+        wait_or_abort(&b_full[s], sph, abort);
+        ++it;
+        // FP32 numerics with the y tile in shared memory: the tensor cores add y too.
+        const bool add_y = MODE == kFp32 && y_unit(p, sc.run, offs[blk.slice] + blk.c0).mode != kYDirect;
+        if (add_y) wait_or_abort(&y_full[s], sph, abort);
         const int tb = tcount & 1;
         wait_or_abort(&t_empty[tb], (uint32_t(tcount >> 1) & 1u) ^ 1u, abort);
         ++tcount;
@@ -671,15 +920,30 @@ __global__ void __launch_bounds__(kExpandThreads, 1) prefill_expand_kernel(const
         tc_fence_after();
         const uint32_t d = tmem + uint32_t(tb * kNT);
         const uint32_t zh = smem_u32(ztile + zb * 2 * kXTileBytes);
-        const uint64_t bd = sw128_desc(smem_u32(btile + bs * kBTileBytes));
+        // K steps of 16: the bucket's (boxed B rows) or 4 (rows padded to 64).
+        const int kb = sc.kb, ksteps = kb ? kb >> 4 : 4;
+        const uint32_t bsa = smem_u32(btile + s * kBTileBytes);
+        const uint64_t bd = kb ? swrow_desc(bsa, 2 * kb) : sw128_desc(bsa);
         const uint64_t ah = sw128_desc(zh), al = sw128_desc(zh + kXTileBytes);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) tc_mma(d, ah + 2 * k, bd + 2 * k, idesc, k > 0 ? 1u : 0u);
+        for (int k = 0; k < 4; ++k)
+          if (k < ksteps) tc_mma(d, ah + 2 * k, bd + 2 * k, idesc, k > 0 ? 1u : 0u);
         if (MODE == kFp32) {
 #pragma unroll
-          for (int k = 0; k < 4; ++k) tc_mma(d, al + 2 * k, bd + 2 * k, idesc, 1u);
+          for (int k = 0; k < 4; ++k)
+            if (k < ksteps) tc_mma(d, al + 2 * k, bd + 2 * k, idesc, 1u);
         }
-        tc_commit(&b_empty[bs]);
+        if (add_y) {
+          // D[:, 64j + n] += sum_k Y_j[:, k] I[n, k]: M = 128, N = 64, K = 64 per box.
+          const uint64_t id = sw128_desc(smem_u32(ident));
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const uint64_t yd = sw128_desc(smem_u32(ytile + s * kYTileBytes + j * kXTileBytes));
+#pragma unroll
+            for (int k = 0; k < 4; ++k) tc_mma(d + uint32_t(64 * j), yd + 2 * k, id + 2 * k, idesc64, 1u);
+          }
+        }
+        tc_commit(&b_empty[s]);
         tc_commit(&t_full[tb]);
       }
       // Every MMA has retired before the TMEM columns are released.
@@ -691,81 +955,180 @@ __global__ void __launch_bounds__(kExpandThreads, 1) prefill_expand_kernel(const
     const int quarter = warp & 3, half = warp >> 2;
     const int row = quarter * 32 + lane;
     const bool vec_ok = (reinterpret_cast<uintptr_t>(p.y) & 15) == 0 && (p.y_stride & 7) == 0;
-    int tcount = 0;
+    int it = 0, tcount = 0;
+    SegCache sc;
     for (int u = u0; u < u1; ++u) {
       const int seg = u / nb;
       const Block blk = block_of(offs, p.S, u - seg * nb);
-      const PSeg si = prefill_segment(p, seg);
+      const PSeg& si = sc.get(p, seg);
       if (!si.ok || blk.slice < 0) continue;
+      const int s = it % kEStages;
+      const uint32_t yph = uint32_t(it / kEStages) & 1u;
+      ++it;
       const int tb = tcount & 1;
       const uint32_t tph = uint32_t(tcount >> 1) & 1u;
       ++tcount;
-      int tok = -1;
-      if (row < si.n) {
-        tok = p.perm[si.pos0 + row];
-        if (tok < 0 || tok >= p.T) tok = -1;
-      }
-      const int cl = blk.c0 + half * 128;            // first column of this half, in the slice
-      const int ncols = min(128, blk.width - cl);    // columns of this half (may be <= 0)
-      const int gcol = offs[blk.slice] + cl;
-      uint16_t* yrow = tok >= 0 ? p.y + int64_t(tok) * p.y_stride + gcol : nullptr;
-      const bool vec = yrow && ncols == 128 && vec_ok && (gcol & 7) == 0;
-      // The old y of this half row is fetched before the MMA completes.
-      uint4 yv[16];
-      if (vec) {
+      const int gcol0 = offs[blk.slice] + blk.c0;
+      const int cl = half * 64;                                // first column of this half
+      const int ncols = min(64, min(kNT, blk.width - blk.c0) - cl);  // may be <= 0
+      const YUnit yu = y_unit(p, sc.run, gcol0);
+      const uint32_t tbase = tmem + (uint32_t(quarter * 32) << 16) + uint32_t(tb * kNT + cl);
+      bool ok;
+      if (yu.mode != kYDirect) {
+        // y tile in shared memory: row `row`, 16-byte chunks 0..7 of box `half`, updated in
+        // place.  FP32 numerics: the accumulator already holds y + delta (the MMA thread
+        // added the y tile) and only its BF16 rounding goes back.  Reference numerics: the
+        // eight old chunks are read before the accumulator is.
+        const bool live = row < si.n && ncols > 0;
+        const uint32_t ybox = smem_u32(ytile + s * kYTileBytes + half * kXTileBytes);
+        if (MODE == kFp32) {
+          ok = __all_sync(0xffffffffu, wait_or_abort(&t_full[tb], tph, abort));  // tcgen05.ld is warp-wide
+          if (ok) {
+            tc_fence_after();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) yv[i] = *reinterpret_cast<const uint4*>(yrow + 8 * i);
-      }
-      if (!wait_or_abort(&t_full[tb], tph, abort)) break;
-      tc_fence_after();
-      const uint32_t tbase = tmem + (uint32_t(quarter * 32) << 16) + uint32_t(tb * kNT + half * 128);
+            for (int ch = 0; ch < 2; ++ch) {
+              uint32_t r[32];
+              tc_ld32(tbase + 32 * ch, r);
+              if (live) {
 #pragma unroll
-      for (int ch = 0; ch < 4; ++ch) {
-        uint32_t r[32];
-        tc_ld32(tbase + 32 * ch, r);
+                for (int i = 0; i < 4; ++i) {
+                  const uint32_t* q = r + 8 * i;
+                  sts16(ybox + swz(row, 4 * ch + i),
+                        make_uint4(cvt_bf16x2(__uint_as_float(q[0]), __uint_as_float(q[1])),
+                                   cvt_bf16x2(__uint_as_float(q[2]), __uint_as_float(q[3])),
+                                   cvt_bf16x2(__uint_as_float(q[4]), __uint_as_float(q[5])),
+                                   cvt_bf16x2(__uint_as_float(q[6]), __uint_as_float(q[7]))));
+                }
+              }
+            }
+            fence_async_smem();  // before a later TMA load rewrites the stage
+          }
+        } else {
+          ok = wait_or_abort(&y_full[s], yph, abort);
+          uint4 yv[8];
+          if (ok && live) {
+#pragma unroll
+            for (int c = 0; c < 8; ++c) yv[c] = lds16(ybox + swz(row, c));
+          }
+          ok = wait_or_abort(&t_full[tb], tph, abort) && ok;
+          ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-wide
+          if (ok) {
+            tc_fence_after();
+#pragma unroll
+            for (int ch = 0; ch < 2; ++ch) {
+              uint32_t r[32];
+              tc_ld32(tbase + 32 * ch, r);
+              if (live) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                  sts16(ybox + swz(row, 4 * ch + i), y_update<MODE>(yv[4 * ch + i], r + 8 * i, si.scale));
+              }
+            }
+            fence_async_smem();  // before a later TMA load rewrites the stage
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&t_empty[tb]);
+        // Once every row is updated, the tile goes back to y: thread i of 256 stores the
+        // 16-byte chunks i, i + 256, ... (rows of 16 chunks, so a warp writes two rows'
+        // 256 contiguous bytes per step).
+        mbar_arrive(&y_done[s]);
+        ok = wait_or_abort(&y_done[s], yph, abort) && ok;
+        // Thread tid's chunk column is tid & 15 and its rows (tid >> 4) + 16k; the
+        // tokens and the chunks are all read before the first store.
+        const int cols = min(kNT, blk.width - blk.c0);
+        const int cc = tid & 15, col = 8 * cc;
+        bool released = false;
+        if (ok && col < cols) {
+          const int* trow = tokrow + s * kTileM;
+          const uint32_t ysrc = smem_u32(ytile + s * kYTileBytes + (cc >> 3) * kXTileBytes);
+          int tk[8];
+          uint4 v[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const int m = (tid >> 4) + 16 * k;
+            tk[k] = m < si.n ? trow[m] : -1;
+          }
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            if (tk[k] >= 0) v[k] = lds16(ysrc + swz((tid >> 4) + 16 * k, cc & 7));
+          mbar_arrive(&y_empty[s]);  // the stage is free once its chunks are in registers
+          released = true;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            if (tk[k] < 0) continue;
+            uint16_t* dst = p.y + int64_t(tk[k]) * p.y_stride + gcol0 + col;
+            if (col + 8 <= cols) {
+              *reinterpret_cast<uint4*>(dst) = v[k];
+            } else {
+              const uint32_t w[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+              for (int e = 0; e < cols - col; ++e) dst[e] = uint16_t(w[e >> 1] >> (16 * (e & 1)));
+            }
+          }
+        }
+        if (!released) mbar_arrive(&y_empty[s]);
+      } else {
+        // Rows gathered through token_indices: old y straight from global memory, fetched
+        // before the MMA completes.
+        int tok = -1;
+        if (row < si.n) {
+          tok = p.perm[si.pos0 + row];
+          if (tok < 0 || tok >= p.T) tok = -1;
+        }
+        const int gcol = gcol0 + cl;
+        uint16_t* yrow = tok >= 0 && ncols > 0 ? p.y + int64_t(tok) * p.y_stride + gcol : nullptr;
+        const bool vec = yrow && ncols == 64 && vec_ok && (gcol & 7) == 0;
+        uint4 yv[8];
         if (vec) {
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const uint4 o = yv[4 * ch + i];
-            const uint32_t ow[4] = {o.x, o.y, o.z, o.w};
-            uint32_t nw[4];
+          for (int i = 0; i < 8; ++i) yv[i] = *reinterpret_cast<const uint4*>(yrow + 8 * i);
+        }
+        ok = __all_sync(0xffffffffu, wait_or_abort(&t_full[tb], tph, abort));
+        if (ok) {
+          tc_fence_after();
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float d0 = __uint_as_float(r[8 * i + 2 * e]), d1 = __uint_as_float(r[8 * i + 2 * e + 1]);
-              const float y0 = __uint_as_float(ow[e] << 16), y1 = __uint_as_float(ow[e] & 0xffff0000u);
-              const float v0 = MODE == kFp32 ? y0 + d0 : y0 + round_through_bf16(d0 * si.scale);
-              const float v1 = MODE == kFp32 ? y1 + d1 : y1 + round_through_bf16(d1 * si.scale);
-              nw[e] = cvt_bf16x2(v0, v1);
+          for (int ch = 0; ch < 2; ++ch) {
+            uint32_t r[32];
+            tc_ld32(tbase + 32 * ch, r);
+            if (vec) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                *reinterpret_cast<uint4*>(yrow + 32 * ch + 8 * i) = y_update<MODE>(yv[4 * ch + i], r + 8 * i, si.scale);
+            } else if (yrow) {
+              for (int j = 0; j < 32; ++j) {
+                const int c = 32 * ch + j;
+                if (c >= ncols) break;
+                const float d = __uint_as_float(r[j]);
+                const float y0 = bf16_bits_to_float(yrow[c]);
+                const float v = MODE == kFp32 ? y0 + d : y0 + round_through_bf16(d * si.scale);
+                yrow[c] = uint16_t(float_to_bf16_bits(v));
+              }
             }
-            *reinterpret_cast<uint4*>(yrow + 32 * ch + 8 * i) = make_uint4(nw[0], nw[1], nw[2], nw[3]);
-          }
-        } else if (yrow) {
-          for (int j = 0; j < 32; ++j) {
-            const int c = 32 * ch + j;
-            if (c >= ncols) break;
-            const float d = __uint_as_float(r[j]);
-            const float y0 = bf16_bits_to_float(yrow[c]);
-            const float v = MODE == kFp32 ? y0 + d : y0 + round_through_bf16(d * si.scale);
-            yrow[c] = uint16_t(float_to_bf16_bits(v));
           }
         }
       }
-      tc_fence_before();
-      mbar_arrive(&t_empty[tb]);
+      if (yu.mode == kYDirect) {
+        // The stage's barriers complete their phase for this unit all the same.
+        tc_fence_before();
+        mbar_arrive(&t_empty[tb]);
+        mbar_arrive(&y_done[s]);
+        mbar_arrive(&y_empty[s]);
+      }
+      if (!ok) break;
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 10) {
+  if (warp == 11) {
     tc_fence_after();
-    tc_dealloc(tmem, 512);
+    tc_dealloc(tmem, 2 * kNT);
   }
 }
 
 // ====================================================================== host side
 struct PrefillLayout {
   int rpad, kparts;
-  int64_t partial, zfinal, counters, total;  // offsets in floats
+  int64_t partial, total;  // offsets in floats
 };
 
 inline PrefillLayout prefill_layout(int64_t tokens, int64_t width, int num_slices, int capacity) {
@@ -774,10 +1137,9 @@ inline PrefillLayout prefill_layout(int64_t tokens, int64_t width, int num_slice
   const int cap = capacity < kMaxRank ? capacity : kMaxRank;
   l.rpad = (num_slices * cap + 15) / 16 * 16;
   l.kparts = int((width + kPartLen - 1) / kPartLen);
+  l.kparts = l.kparts < kMaxParts ? l.kparts : kMaxParts;
   l.partial = 0;
-  l.zfinal = l.partial + int64_t(l.kparts) * T * l.rpad;
-  l.counters = l.zfinal + T * l.rpad;
-  l.total = l.counters + (T + 3) / 4 * 4;
+  l.total = l.partial + int64_t(l.kparts) * T * l.rpad;
   return l;
 }
 
@@ -880,9 +1242,8 @@ extern "C" int lf_sgmv_prefill(
   PParams p{static_cast<const uint16_t*>(x), x_stride, static_cast<const uint16_t*>(a),
             static_cast<const uint16_t*>(b), b_offsets, b_strides, static_cast<uint16_t*>(y),
             y_stride, segment_indptr, segment_slots, token_indices, ranks, scales, slice_offsets,
-            segment_count, workspace + l.partial, workspace + l.zfinal,
-            reinterpret_cast<int*>(workspace + l.counters), int(T), int(width), out_width,
-            num_slices, capacity, num_slots, max_segments, l.rpad, l.kparts, numerics, 0};
+            segment_count, workspace + l.partial, int(T), int(width), out_width, num_slices, capacity,
+            num_slots, max_segments, l.rpad, l.kparts, 2 * sms, numerics, 0};
   {
     // x [T, K] and A [slots*S*cap, K] as 2-D tensors for the shrink's TMA boxes.
     const PFN_cuTensorMapEncodeTiled_v12000 encode = prefill_tensor_map_encoder();
@@ -890,17 +1251,47 @@ extern "C" int lf_sgmv_prefill(
     const cuuint32_t estr[2] = {1, 1};
     const cuuint64_t xdims[2] = {cuuint64_t(width), cuuint64_t(T)};
     const cuuint64_t xstrides[1] = {cuuint64_t(x_stride) * 2};
-    const cuuint32_t xbox[2] = {64, kTileM};
     const cuuint64_t adims[2] = {cuuint64_t(width), cuuint64_t(num_slots) * num_slices * capacity};
     const cuuint64_t astrides[1] = {cuuint64_t(width) * 2};
     const cuuint32_t abox[2] = {64, cuuint32_t(l.rpad)};
-    CUresult r = encode(&p.tmap_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), xdims,
-                        xstrides, xbox, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = CUDA_SUCCESS;
+    for (int h = 0; h < 5 && r == CUDA_SUCCESS; ++h) {
+      const cuuint32_t xbox[2] = {64u, cuuint32_t(kTileM >> h)};
+      r = encode(&p.tmap_x[h], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), xdims, xstrides, xbox,
+                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    }
     if (r == CUDA_SUCCESS)
       r = encode(&p.tmap_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(a), adims, astrides,
                  abox, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    // The compact B per bucket 16 / 32 / 64, boxes of 128 and 16 rows.
+    for (int m = 0; m < 3 && r == CUDA_SUCCESS; ++m) {
+      const int kb = 16 << m;
+      const cuuint64_t bdims[2] = {cuuint64_t(kb), cuuint64_t(kBRowsNominal)};
+      const cuuint64_t bstrides[1] = {cuuint64_t(kb) * 2};
+      const CUtensorMapSwizzle sw =
+          m == 0 ? CU_TENSOR_MAP_SWIZZLE_32B : m == 1 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
+      for (int h = 0; h < 2 && r == CUDA_SUCCESS; ++h) {
+        const cuuint32_t bbox[2] = {cuuint32_t(kb), h == 0 ? 128u : 16u};
+        r = encode(&p.tmap_b[m][h], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(b), bdims, bstrides,
+                   bbox, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      }
+    }
+    // y [T, N] for the expand's tile loads and stores, when its layout allows TMA.
+    if (aligned16(y) && y_stride % 8 == 0) p.y_mode = 1;
+    if (r == CUDA_SUCCESS && p.y_mode && out_width >= 64 && T >= kTileM) {
+      const cuuint64_t ydims[2] = {cuuint64_t(out_width), cuuint64_t(T)};
+      const cuuint64_t ystrides[1] = {cuuint64_t(y_stride) * 2};
+      for (int h = 0; h < 5 && r == CUDA_SUCCESS; ++h) {
+        const cuuint32_t ybox[2] = {64u, cuuint32_t(kTileM >> h)};
+        r = encode(&p.tmap_y[h], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, y, ydims, ystrides, ybox, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      }
+      p.y_mode |= 2;
+    }
     if (r != CUDA_SUCCESS) return fail(LF_E_CUDA, "sgmv_prefill: cuTensorMapEncodeTiled failed");
   }
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -916,7 +1307,10 @@ extern "C" int lf_sgmv_prefill(
       return rc;
   }
   {
-    const int smem = kBStages * kBTileBytes + 4 * kXTileBytes + 1024 + 256;
+    // Tiles and the identity, then 24 barriers, TMEM slot, slice offsets and abort word
+    // (< 320 bytes), then the stages' row tokens.
+    const int smem =
+        kEStages * (kYTileBytes + kBTileBytes) + 4 * kXTileBytes + kIdentBytes + 1024 + 320 + kEStages * kTileM * 4;
     auto kernel = numerics == kFp32 ? prefill_expand_kernel<kFp32> : prefill_expand_kernel<kReference>;
     static int flags[2][64] = {};
     if (int rc = ensure_smem(kernel, smem, flags[numerics])) return rc;

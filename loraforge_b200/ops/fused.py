@@ -102,9 +102,12 @@ def lora_shrink_expand_prefill(
 ) -> None:
     """``lora_shrink_expand`` for prefill batches: segments of up to 128 tokens.
 
-    Route with ``group_tokens(..., chunk=128)``.  Every segment runs on the tcgen05 tensor
-    cores (128-token tiles, FP32 accumulators in TMEM; a short segment leaves tile rows
-    idle but moves no extra x or y bytes).  Same operands, numerics and workspace rules
+    Route with ``group_tokens(..., chunk=128, runs=True)``: segments that are one run of
+    tokens move their y rows as 2-D TMA tiles; segments gathered from several runs (a
+    plain ``chunk=128`` grouping, or a serving framework's chunks) are correct too, with
+    their y rows copied row by row.  Every segment runs on the tcgen05 tensor cores
+    (128-token tiles, FP32 accumulators in TMEM; a short segment leaves tile rows idle but
+    moves no extra x or y bytes).  Same operands, numerics and workspace rules
     as ``lora_shrink_expand`` with ``prefill_workspace_floats`` for the size.  The B200
     form of the reference's prefill SGMV (the rank-aware shrink,
     src/loraforge/integrations/_sglang_rank_aware.py:14-171, and the chunked expand it

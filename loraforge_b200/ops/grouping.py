@@ -35,11 +35,17 @@ def empty_routing(num_tokens: int, device) -> Routing:
     )
 
 
-def group_tokens(slots, num_slots: int, *, chunk: int = 16, out: Routing | None = None) -> Routing:
+def group_tokens(
+    slots, num_slots: int, *, chunk: int = 16, runs: bool = False, out: Routing | None = None
+) -> Routing:
     """Group tokens by ``slots`` (int32 [T], -1 = no adapter) into <= ``chunk`` token segments.
 
-    ``chunk <= 0`` gives one segment per active slot.  Writes into ``out`` when given
-    (every buffer must have room for T tokens), else allocates.
+    ``chunk <= 0`` gives one segment per active slot.  ``runs=True`` cuts every maximal
+    run of consecutive tokens of a slot separately (``lf_split_runs``), so no segment
+    spans a gap in token order: in a prefill batch every segment is then one run of a
+    request's tokens, which the prefill kernels move as 2-D tiles.  The products are the
+    same either way.  Writes into ``out`` when given (every buffer must have room for T
+    tokens), else allocates.
     """
     import torch
 
@@ -64,19 +70,46 @@ def group_tokens(slots, num_slots: int, *, chunk: int = 16, out: Routing | None 
             or buf.numel() < need
         ):
             raise ValueError("routing buffers must be contiguous int32 with room for every token")
+    if type(runs) is not bool:
+        raise ValueError("runs must be a bool")
+    # With runs, the slot-ordered grouping goes to temporaries first (token_indices
+    # straight to its final buffer), then is cut at the gaps into ``out``.
+    first = out
+    if runs:
+        first = Routing(
+            torch.empty(T + 1, dtype=torch.int32, device=slots.device),
+            torch.empty(max(1, T), dtype=torch.int32, device=slots.device),
+            out.token_indices,
+            torch.empty(1, dtype=torch.int32, device=slots.device),
+        )
     with torch.cuda.device(slots.device):
+        stream = _native.stream_of(slots.device)
         _native.call(
             "lf_group_tokens",
             slots.data_ptr(),
             T,
             num_slots,
             chunk,
-            out.segment_indptr.data_ptr(),
-            out.segment_slots.data_ptr(),
-            out.token_indices.data_ptr(),
-            out.segment_count.data_ptr(),
-            _native.stream_of(slots.device),
+            first.segment_indptr.data_ptr(),
+            first.segment_slots.data_ptr(),
+            first.token_indices.data_ptr(),
+            first.segment_count.data_ptr(),
+            stream,
         )
+        if runs:
+            _native.call(
+                "lf_split_runs",
+                first.segment_indptr.data_ptr(),
+                first.segment_slots.data_ptr(),
+                first.token_indices.data_ptr(),
+                first.segment_count.data_ptr(),
+                T,
+                chunk,
+                out.segment_indptr.data_ptr(),
+                out.segment_slots.data_ptr(),
+                out.segment_count.data_ptr(),
+                stream,
+            )
     return out
 
 

@@ -112,3 +112,69 @@ def test_segment_routes_ignores_padded_segments():
     routes = segment_routes(indptr, seg_slots, perm, count, 5)
     torch.cuda.synchronize()
     assert routes.tolist() == [5, 7, -1, 5, -1]
+
+
+def split_runs_reference(indptr, seg_slots, perm, chunk):
+    """Segments of the same grouping cut at every gap in token order, each run into pieces
+    of at most `chunk` tokens from its own start (chunk <= 0: one piece per run)."""
+    out_indptr, out_slots = [], []
+    for s in range(len(seg_slots)):
+        if s > 0 and seg_slots[s - 1] == seg_slots[s]:
+            continue  # the slot's range was handled from its first segment
+        e = s
+        while e + 1 < len(seg_slots) and seg_slots[e + 1] == seg_slots[s]:
+            e += 1
+        lo, hi = int(indptr[s]), int(indptr[e + 1])
+        p = lo
+        while p < hi:
+            q = p + 1
+            while q < hi and perm[q] == perm[q - 1] + 1:
+                q += 1
+            step = chunk if chunk > 0 else q - p
+            for a in range(p, q, step):
+                out_indptr.append(a)
+                out_slots.append(int(seg_slots[s]))
+            p = q
+    out_indptr.append(int(indptr[len(seg_slots)]))
+    return out_indptr, out_slots
+
+
+def check_runs(slots_np, num_slots, chunk):
+    slots = torch.tensor(slots_np, dtype=torch.int32, device="cuda")
+    routing = group_tokens(slots, num_slots, chunk=chunk, runs=True)
+    torch.cuda.synchronize()
+    indptr, seg_slots, perm, _ = ref.group_tokens(slots_np, num_slots, chunk)
+    want_indptr, want_slots = split_runs_reference(indptr, seg_slots, perm, chunk)
+    count = int(routing.segment_count.item())
+    assert count == len(want_slots)
+    assert routing.segment_indptr[: count + 1].tolist() == want_indptr
+    assert routing.segment_slots[:count].tolist() == want_slots
+    assert routing.token_indices[: len(slots_np)].tolist() == perm.tolist()
+    # Every segment is one run of one slot, at most `chunk` tokens.
+    ind = routing.segment_indptr[: count + 1].cpu().numpy()
+    tok = routing.token_indices.cpu().numpy()
+    for s in range(count):
+        run = tok[ind[s] : ind[s + 1]]
+        assert len(run) >= 1 and (chunk <= 0 or len(run) <= chunk)
+        assert np.all(np.diff(run) == 1)
+        assert np.all(slots_np[run] == routing.segment_slots[s].item())
+
+
+@pytest.mark.parametrize("chunk", [0, 5, 16, 128])
+@pytest.mark.parametrize("seed", range(3))
+def test_split_runs_prefill_batches(seed, chunk):
+    # Requests of geometric lengths, adapters drawn with repeats, some without adapter.
+    rng = np.random.default_rng(100 + seed)
+    num_slots = int(rng.integers(2, 40))
+    lengths = np.maximum(1, rng.geometric(1 / 200, size=int(rng.integers(1, 60))))
+    owners = rng.integers(-1, num_slots, size=len(lengths))
+    check_runs(np.repeat(owners, lengths), num_slots, chunk)
+
+
+@pytest.mark.parametrize("chunk", [0, 3, 16])
+def test_split_runs_scattered_and_edge_cases(chunk):
+    rng = np.random.default_rng(7)
+    check_runs(rng.integers(-2, 9, size=5000), 8, chunk)  # decode-like: many one-token runs
+    check_runs(np.full(1, 3), 4, chunk)
+    check_runs(np.full(300, -1), 4, chunk)  # no active token: no segment
+    check_runs(np.arange(70) % 2, 2, chunk)  # every run one token long

@@ -48,9 +48,9 @@ def prefill_case(lengths, slots=16, k=1024, widths=(1024,), ranks=None, seed=0, 
     return x.to(dev), a.to(dev), b.to(dev), base.to(dev), slots_t, meta, S
 
 
-def routed(meta, slots_t, num_slots, chunk):
+def routed(meta, slots_t, num_slots, chunk, runs=False):
     out = dict(meta)
-    out.update(zip(ROUTING_KEYS, group_tokens(slots_t, num_slots, chunk=chunk)))
+    out.update(zip(ROUTING_KEYS, group_tokens(slots_t, num_slots, chunk=chunk, runs=runs)))
     return out
 
 
@@ -83,11 +83,15 @@ def test_long_and_short_segments_fp32_gate():
     assert torch.equal(out.cpu()[inactive], base.cpu()[inactive])
 
 
-def test_config3_shapes():
-    # BASELINE config 3 shapes on a smaller batch: K = N = 5120, rank 64.
-    lengths = geometric(np.random.default_rng(2), 8, 256, total=1024)
-    x, a, b, base, slots_t, meta, S = prefill_case(lengths, k=5120, widths=(5120,), seed=2, inactive=0.0)
-    meta = routed(meta, slots_t, 16, 128)
+@pytest.mark.parametrize("runs", [False, True])
+def test_config3_shapes(runs):
+    # BASELINE config 3 shapes on a smaller batch: K = N = 5120, rank 64; requests share
+    # adapters, so the plain grouping has segments gathered from two runs and the run
+    # grouping (the bench's) has none.
+    lengths = geometric(np.random.default_rng(2), 16, 256, total=2048)
+    x, a, b, base, slots_t, meta, S = prefill_case(lengths, slots=6, k=5120, widths=(5120,), seed=2,
+                                                   inactive=0.0)
+    meta = routed(meta, slots_t, 6, 128, runs=runs)
     out = run_prefill(x, a, b, base.clone(), meta, S)
     expected = fp32_reference(x, a, b, base, slots_t, meta, S)
     gate = ref.fp32_gate(values(bf16_bits(out)), expected)
@@ -101,6 +105,70 @@ def test_mixed_ranks_small_buckets_and_slices():
         lengths, k=1024, widths=(768, 256, 256), ranks=ranks, seed=3
     )
     meta = routed(meta, slots_t, len(ranks), 128)
+    out = run_prefill(x, a, b, base.clone(), meta, S)
+    expected = fp32_reference(x, a, b, base, slots_t, meta, S)
+    gate = ref.fp32_gate(values(bf16_bits(out)), expected)
+    assert gate["excess"] <= 1e-2, gate
+
+
+def shifted_store(ranks, n, gen, shifted=()):
+    """Compact B with every region 64-element aligned, except that the slots in `shifted`
+    start 8 elements later (an offset that is not a whole number of bucket rows)."""
+    pieces, offsets, strides, cursor = [], [], [], 0
+    for i, r in enumerate(ranks):
+        bucket = 1 << (max(1, r) - 1).bit_length()
+        pad = (-cursor) % 64 + (8 if i in shifted else 0)
+        pieces.append(torch.zeros(pad, dtype=torch.bfloat16))
+        cursor += pad
+        w = (torch.randn(n, bucket, generator=gen) / max(r, 1) ** 0.5).bfloat16()
+        w[:, r:] = 0
+        offsets.append(cursor)
+        strides.append(bucket)
+        pieces.append(w.flatten())
+        cursor += w.numel()
+    return torch.cat(pieces), offsets, strides
+
+
+def test_ragged_blocks_and_unaligned_b_offsets():
+    # B rows of buckets 16 / 32 / 64 arrive in TMA boxes of 128 and 16 rows plus a cp.async
+    # tail.  Slice widths 1000 / 124 / 12 leave partial 256-column blocks: 232 rows (one
+    # 128-row box, six 16-row boxes, 8 tail rows), 124 (seven 16-row boxes, 12 tail rows)
+    # and 12 (tail rows alone).  Slots 0 and 3 have B offsets that are not a whole number of
+    # rows and take the cp.async path for every row.
+    ranks = [16, 32, 64, 64, 12, 20, 40, 64]
+    widths = (1000, 124, 12)
+    lengths = geometric(np.random.default_rng(8), 32, 40)
+    x, a, _, base, slots_t, meta, S = prefill_case(
+        lengths, slots=len(ranks), k=1024, widths=widths, ranks=ranks, seed=8, inactive=0.05
+    )
+    assert set(range(len(ranks))) <= set(slots_t.cpu().tolist())
+    b, offsets, _ = shifted_store(ranks, sum(widths), torch.Generator().manual_seed(17), shifted={0, 3})
+    assert offsets[0] % 16 and offsets[3] % 64 and not offsets[2] % 64
+    b = b.cuda()
+    meta["b_offsets"] = torch.tensor(offsets, dtype=torch.int64, device="cuda")
+    meta = routed(meta, slots_t, len(ranks), 128)
+    for numerics in ("fp32", "reference"):
+        out = run_prefill(x, a, b, base.clone(), meta, S, numerics)
+        if numerics == "fp32":
+            expected = fp32_reference(x, a, b, base, slots_t, meta, S)
+            gate = ref.fp32_gate(values(bf16_bits(out)), expected)
+            assert gate["excess"] <= 1e-2, gate
+        else:
+            want = base.clone()
+            lora_shrink_expand(x, a, b, want, **routed(meta, slots_t, len(ranks), 16), num_slices=S,
+                               numerics="reference")
+            torch.cuda.synchronize()
+            g, w = bf16_bits(out), bf16_bits(want)
+            assert rel_l2(values(g), values(w)) < 0.005
+            assert np.mean(g == w) > 0.95
+
+
+def test_batch_under_one_tile_of_tokens():
+    # Fewer than 128 tokens: y has no tensor maps and every row is read and written by the
+    # epilogue threads themselves.
+    lengths = np.array([5, 40, 17, 30, 3], dtype=np.int64)
+    x, a, b, base, slots_t, meta, S = prefill_case(lengths, k=1024, widths=(512, 128), seed=9, inactive=0.0)
+    meta = routed(meta, slots_t, 16, 128)
     out = run_prefill(x, a, b, base.clone(), meta, S)
     expected = fp32_reference(x, a, b, base, slots_t, meta, S)
     gate = ref.fp32_gate(values(bf16_bits(out)), expected)
