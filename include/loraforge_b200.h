@@ -55,6 +55,19 @@ int lf_group_tokens(const int32_t* slots, int64_t num_tokens, int32_t num_slots,
                     int32_t* token_indices, int32_t* segment_count, void* stream);
 
 /*
+ * lf_group_tokens followed by lf_split_runs' cut, in one launch when the batch allows it
+ * (64..65535 tokens and the slot tables in shared memory): the same token_indices, and
+ * segments that are runs of consecutive tokens of one slot, each cut into pieces of at
+ * most `chunk` tokens from the run's start.  Larger batches take the two kernels, with
+ * the slot-ordered tables in `scratch` (2T + 2 ints; may be NULL when the one-launch form
+ * applies).
+ */
+int lf_group_token_runs(const int32_t* slots, int64_t num_tokens, int32_t num_slots,
+                        int32_t chunk, int32_t* segment_indptr, int32_t* segment_slots,
+                        int32_t* token_indices, int32_t* segment_count, int32_t* scratch,
+                        void* stream);
+
+/*
  * Re-chunks a grouping (lf_group_tokens' tables) so that no segment spans a gap in token
  * order: inside each slot's range of token_indices, every maximal run of consecutive
  * tokens is cut into pieces of at most `chunk` tokens from its own start (chunk <= 0:

@@ -41,7 +41,7 @@ def group_tokens(
     """Group tokens by ``slots`` (int32 [T], -1 = no adapter) into <= ``chunk`` token segments.
 
     ``chunk <= 0`` gives one segment per active slot.  ``runs=True`` cuts every maximal
-    run of consecutive tokens of a slot separately (``lf_split_runs``), so no segment
+    run of consecutive tokens of a slot separately (``lf_group_token_runs``), so no segment
     spans a gap in token order: in a prefill batch every segment is then one run of a
     request's tokens, which the prefill kernels move as 2-D tiles.  The products are the
     same either way.  Writes into ``out`` when given (every buffer must have room for T
@@ -72,41 +72,35 @@ def group_tokens(
             raise ValueError("routing buffers must be contiguous int32 with room for every token")
     if type(runs) is not bool:
         raise ValueError("runs must be a bool")
-    # With runs, the slot-ordered grouping goes to temporaries first (token_indices
-    # straight to its final buffer), then is cut at the gaps into ``out``.
-    first = out
-    if runs:
-        first = Routing(
-            torch.empty(T + 1, dtype=torch.int32, device=slots.device),
-            torch.empty(max(1, T), dtype=torch.int32, device=slots.device),
-            out.token_indices,
-            torch.empty(1, dtype=torch.int32, device=slots.device),
-        )
     with torch.cuda.device(slots.device):
         stream = _native.stream_of(slots.device)
-        _native.call(
-            "lf_group_tokens",
-            slots.data_ptr(),
-            T,
-            num_slots,
-            chunk,
-            first.segment_indptr.data_ptr(),
-            first.segment_slots.data_ptr(),
-            first.token_indices.data_ptr(),
-            first.segment_count.data_ptr(),
-            stream,
-        )
         if runs:
+            # One launch for most batches; larger ones stage the slot-ordered tables in
+            # the scratch vector before the run cut.
+            scratch = torch.empty(2 * T + 2, dtype=torch.int32, device=slots.device)
             _native.call(
-                "lf_split_runs",
-                first.segment_indptr.data_ptr(),
-                first.segment_slots.data_ptr(),
-                first.token_indices.data_ptr(),
-                first.segment_count.data_ptr(),
+                "lf_group_token_runs",
+                slots.data_ptr(),
                 T,
+                num_slots,
                 chunk,
                 out.segment_indptr.data_ptr(),
                 out.segment_slots.data_ptr(),
+                out.token_indices.data_ptr(),
+                out.segment_count.data_ptr(),
+                scratch.data_ptr(),
+                stream,
+            )
+        else:
+            _native.call(
+                "lf_group_tokens",
+                slots.data_ptr(),
+                T,
+                num_slots,
+                chunk,
+                out.segment_indptr.data_ptr(),
+                out.segment_slots.data_ptr(),
+                out.token_indices.data_ptr(),
                 out.segment_count.data_ptr(),
                 stream,
             )

@@ -178,3 +178,6 @@ def test_split_runs_scattered_and_edge_cases(chunk):
     check_runs(np.full(1, 3), 4, chunk)
     check_runs(np.full(300, -1), 4, chunk)  # no active token: no segment
     check_runs(np.arange(70) % 2, 2, chunk)  # every run one token long
+    # Past the one-launch form's 65535 tokens: grouping into the scratch tables, then the cut.
+    lengths = np.maximum(1, rng.geometric(1 / 900, size=90))
+    check_runs(np.repeat(rng.integers(-1, 12, size=len(lengths)), lengths)[:70000], 12, chunk)
