@@ -40,10 +40,13 @@
 
 #include "launch.cuh"
 #include "sgmv.cuh"
+#include "tcgen05.cuh"
 #include "tma.cuh"
 
 namespace lfb {
 namespace {
+
+using namespace tc;
 
 constexpr int kTileM = 128;                  // tokens per tile (UMMA M)
 constexpr int kRowBytes = 128;               // one swizzled K-major row: 64 BF16
@@ -157,37 +160,6 @@ __device__ __forceinline__ PSeg prefill_segment(const PParams& p, int seg) {
   return s;
 }
 
-// ------------------------------------------------------------------ tcgen05 wrappers
-__device__ __forceinline__ void tc_alloc(uint32_t* slot, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
-               "r"(ncols)
-               : "memory");
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tc_dealloc(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-// D[tmem] (+)= A[smem desc] . B[smem desc]^T, kind::f16 (BF16 in, FP32 accumulate).
-__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
-                                       uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
-      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// Arrive once on `bar` when every tcgen05 operation this thread issued has completed.
-__device__ __forceinline__ void tc_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   smem_u32(bar))
-               : "memory");
-}
 // 128 producer/epilogue threads of the shrink: true if any of them passed `v` (barrier 2).
 __device__ __forceinline__ bool any128(bool v) {
   uint32_t r;
@@ -198,86 +170,6 @@ __device__ __forceinline__ bool any128(bool v) {
       : "r"(v ? 1u : 0u)
       : "memory");
   return r != 0;
-}
-
-// Bounded mbarrier wait that records an expiry in the CTA's abort word; later waits are
-// skipped once the word is set, so a broken pipeline ends in bounded time.
-__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort) {
-  if (*abort) return false;
-  if (mbar_wait(bar, parity)) return true;
-  *abort = 1;
-  return false;
-}
-
-// Thread i of the warp receives TMEM lane (lane field of taddr) + i, 16 / 32 columns;
-// the load is waited for inside the same asm block, so the registers are final on exit.
-__device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
-      "tcgen05.wait::ld.sync.aligned;"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-}
-__device__ __forceinline__ void tc_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
-      "tcgen05.wait::ld.sync.aligned;"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-}
-
-// Shared-memory descriptor of a K-major tile with 128-byte rows, 128-byte swizzle and
-// 8-row groups 1024 bytes apart (tile base 1024-byte aligned).  Advancing the start
-// address by 32 bytes selects the next 16-element K step.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-  return uint64_t((saddr & 0x3FFFFu) >> 4) | (uint64_t(16 >> 4) << 16) | (uint64_t(1024 >> 4) << 32) |
-         (uint64_t(1) << 46) | (uint64_t(2) << 61);
-}
-
-// The same for rows of 32, 64 or 128 bytes (bucket 16 / 32 / 64 BF16) swizzled by their
-// own size (layout type 6 / 4 / 2), 8-row groups 8 rows apart.
-__device__ __forceinline__ uint64_t swrow_desc(uint32_t saddr, int row_bytes) {
-  const uint64_t type = row_bytes == 128 ? 2 : row_bytes == 64 ? 4 : 6;
-  return uint64_t((saddr & 0x3FFFFu) >> 4) | (uint64_t(16 >> 4) << 16) |
-         (uint64_t((8 * row_bytes) >> 4) << 32) | (uint64_t(1) << 46) | (type << 61);
-}
-
-// Byte offset of 16-byte chunk c of row r in a tile of row_bytes-byte rows swizzled by
-// row_bytes (address bits 4.. XOR bits 7..; tile base aligned to 8 rows).
-__device__ __forceinline__ uint32_t swz_rows(int r, int c, int row_bytes) {
-  const uint32_t off = uint32_t(r) * uint32_t(row_bytes) + (uint32_t(c) << 4);
-  const uint32_t mask = uint32_t(row_bytes >> 4) - 1u;
-  return off ^ (((off >> 7) & mask) << 4);
-}
-
-// Instruction descriptor, kind::f16: BF16 A and B (K-major), FP32 D, M x N.
-__host__ __device__ constexpr uint32_t idesc_bf16(int m, int n) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
-}
-
-// Byte offset of 16-byte chunk c (elements 8c..8c+7) of row r in a swizzled tile.
-__device__ __forceinline__ uint32_t swz(int r, int c) {
-  return uint32_t(r) * kRowBytes + (uint32_t((c ^ (r & 7)) & 7) << 4);
-}
-
-// 16-byte cp.async; bytes beyond src_bytes (0 or 16 here) are zero-filled.
-__device__ __forceinline__ void cp16(uint32_t dst, const void* src, uint32_t src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
-               : "memory");
-}
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-__device__ __forceinline__ void sts16(uint32_t dst, uint4 v) {
-  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
-               : "memory");
 }
 
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
@@ -292,20 +184,7 @@ __device__ __forceinline__ uint32_t cvt_bf16x2(float first, float second) {
   return r;
 }
 
-__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
-  return p + ((1024u - (smem_u32(p) & 1023u)) & 1023u);
-}
-
 // ====================================================================== shrink
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
-                                            uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, "
-      "{%2, %3}], [%4];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
-      : "memory");
-}
-
 // Stage: x tile (128 rows) then A tile (rpad rows), both K-major with 128-byte rows and
 // 128-byte swizzle.  A arrives as one 2-D TMA box; x too when the chunk's tokens are one
 // contiguous run of rows (the usual prefill case), else each producer thread gathers its
@@ -562,20 +441,6 @@ __device__ __forceinline__ int row_token(const PParams& p, const PSeg& si, const
   if (yu.tok0 >= 0) return yu.tok0 + m;
   const int t = p.perm[si.pos0 + m];
   return t >= 0 && t < p.T ? t : -1;
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
-
-__device__ __forceinline__ uint4 lds16(uint32_t addr) {
-  uint4 v;
-  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "r"(addr)
-               : "memory");
-  return v;
 }
 
 // y + delta for 8 columns: old y (BF16 x 8) and 8 FP32 accumulator values.
