@@ -786,6 +786,36 @@ __device__ __forceinline__ void expand_stage_pair(const Params& p, const ExpandH
   }
 }
 
+// First expand unit of part `part` of `parts` parts of equal estimated cost.  A unit
+// (segment s, 128 columns) costs kUnitCost + n_s, measured in units of one token row
+// (per-CTA timestamps of BASELINE config 1: a 512-column stage takes about 1.3 us plus
+// 0.013 us per token row), so the cost before segment s is
+// ncb * (kUnitCost * s + indptr[s] - indptr[0]): monotone in s, found by a 32-way search
+// of the warp (lanes probe evenly spaced segments, the ballot keeps the prefix).
+constexpr int kUnitCost = 24;
+__device__ int expand_cost_split(const Params& p, int nseg, int ncb, int part, int parts, int lane) {
+  if (part <= 0 || nseg <= 0) return 0;
+  if (part >= parts) return nseg * ncb;
+  const int base = p.indptr[0];
+  auto before = [&](int s) { return int64_t(ncb) * (int64_t(kUnitCost) * s + (p.indptr[s] - base)); };
+  const int64_t target = before(nseg) * part / parts;
+  int lo = 0, hi = nseg;  // before(lo) <= target; the answer lies in [lo, hi]
+  while (lo < hi) {
+    const int step = (hi - lo + 31) / 32;
+    const int s = min(hi, lo + step * (lane + 1));
+    const unsigned le = __ballot_sync(0xffffffffu, before(s) <= target);
+    const int k = __popc(le);  // probes at or below the target (a prefix of the lanes)
+    const int next_lo = k > 0 ? min(hi, lo + step * k) : lo;
+    const int next_hi = k < 32 ? min(hi, lo + step * (k + 1) - 1) : hi;
+    lo = next_lo;
+    hi = max(lo, next_hi);
+  }
+  if (lo >= nseg) return nseg * ncb;
+  const int n = p.indptr[lo + 1] - p.indptr[lo];
+  const int64_t unit = (target - before(lo)) / (kUnitCost + max(0, n));
+  return lo * ncb + (unit < ncb ? int(unit) : ncb);
+}
+
 template <int MODE, bool STAGED>
 __global__ void __launch_bounds__(kThreads, 2) sgmv_expand_kernel(const __grid_constant__ Params p) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -809,15 +839,22 @@ __global__ void __launch_bounds__(kThreads, 2) sgmv_expand_kernel(const __grid_c
 
   const int nseg = segment_total(p);
   const int ncb = (p.N + kExpandCols - 1) / kExpandCols;
-  const int total = nseg * ncb;  // fits int32 (checked on the host)
-  const int per = (total + int(gridDim.x) - 1) / int(gridDim.x);
-  const int u0 = int(blockIdx.x) * per;
-  const int u1 = min(total, u0 + per);
-  if (u0 >= u1) return;
 
   if (warp == kConsumerWarps) {
     // ------------------------------------------------------------ producer warp
-    // B rows and y rows do not depend on the shrink: no griddepcontrol.wait here.
+    // B rows and y rows do not depend on the shrink: no griddepcontrol.wait here.  With at
+    // least 32 units per CTA (wide projections: a CTA's units stay within one or two
+    // segments) the units split the batch by estimated cost, not by count (a 16-token
+    // segment's stage costs about half again a 1-token one's: its y rows are copied too);
+    // narrower ones split by count, where the z reload at every segment change a cost
+    // split adds to the light CTAs outweighs the gain (BASELINE config 1 qkv and down).
+    const int total = nseg * ncb;
+    const bool by_cost = total >= 32 * int(gridDim.x);
+    const int per = (total + int(gridDim.x) - 1) / int(gridDim.x);
+    const int u0 = by_cost ? expand_cost_split(p, nseg, ncb, int(blockIdx.x), int(gridDim.x), lane)
+                           : min(total, int(blockIdx.x) * per);
+    const int u1 = by_cost ? expand_cost_split(p, nseg, ncb, int(blockIdx.x) + 1, int(gridDim.x), lane)
+                           : min(total, int(blockIdx.x) * per + per);
     // Consecutive 256-column units of one segment are merged into a stage while its
     // B rows fit kBStage and its columns kStageCols.
     int cur = -1, tok = -1;
