@@ -55,17 +55,17 @@ int lf_group_tokens(const int32_t* slots, int64_t num_tokens, int32_t num_slots,
                     int32_t* token_indices, int32_t* segment_count, void* stream);
 
 /*
- * lf_group_tokens followed by lf_split_runs' cut, in one launch when the batch allows it
- * (64..65535 tokens and the slot tables in shared memory): the same token_indices, and
- * segments that are runs of consecutive tokens of one slot, each cut into pieces of at
- * most `chunk` tokens from the run's start.  Larger batches take the two kernels, with
- * the slot-ordered tables in `scratch` (2T + 2 ints; may be NULL when the one-launch form
- * applies).
+ * Device grouping of a prefill batch by runs, in one launch: a run is a maximal stretch
+ * of consecutive tokens whose slot is in [0, num_slots); each run is cut into segments of
+ * at most `chunk` tokens from its own start (chunk <= 0: one segment per run), in token
+ * order.  token_indices[0:n_active] = the active tokens in token order, then the others;
+ * segment_indptr / segment_slots / segment_count as for lf_group_tokens.  Any
+ * segmentation of the same tokens gives the same products; this one makes every prefill
+ * segment one run of a request's tokens (2-D tiles in lf_sgmv_prefill) and needs no sort.
  */
 int lf_group_token_runs(const int32_t* slots, int64_t num_tokens, int32_t num_slots,
                         int32_t chunk, int32_t* segment_indptr, int32_t* segment_slots,
-                        int32_t* token_indices, int32_t* segment_count, int32_t* scratch,
-                        void* stream);
+                        int32_t* token_indices, int32_t* segment_count, void* stream);
 
 /*
  * Re-chunks a grouping (lf_group_tokens' tables) so that no segment spans a gap in token

@@ -37,7 +37,7 @@ class SliceDesc(ctypes.Structure):
 SIGNATURES = {
     "lf_group_tokens": [_p, _i64, _i32, _i32, _p, _p, _p, _p, _p],
     "lf_split_runs": [_p, _p, _p, _p, _i64, _i32, _p, _p, _p, _p],
-    "lf_group_token_runs": [_p, _i64, _i32, _i32, _p, _p, _p, _p, _p, _p],
+    "lf_group_token_runs": [_p, _i64, _i32, _i32, _p, _p, _p, _p, _p],
     "lf_row_shrink": [_p, _i64, _p, _p, _p, _p, _i64, _i64, _i32, _i32, _i32, _i32, _p],
     "lf_row_expand": [
         _p, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _p,

@@ -184,6 +184,72 @@ __device__ void cut_runs(const int* code, int n, int chunk, int32_t* out_indptr,
   }
 }
 
+// The runs of a batch in token order: a run is a maximal stretch of consecutive tokens
+// with one slot in [0, num_slots), cut into pieces of at most `chunk` tokens from its own
+// start (chunk <= 0: one piece per run); token_indices lists the active tokens in token
+// order, then the others.  One CTA: thread i takes a contiguous stretch of tokens and walks
+// it three times (active count and last run start, its pieces, then its writes), with
+// block scans carrying the counts and the run start in from the left.
+__global__ void __launch_bounds__(kGroupThreads)
+token_runs_kernel(const int32_t* __restrict__ slots, int T, int num_slots, int chunk,
+                  int32_t* __restrict__ indptr, int32_t* __restrict__ seg_slots,
+                  int32_t* __restrict__ perm, int32_t* __restrict__ seg_count) {
+  __shared__ int wtmp[kGroupWarps];
+  __shared__ int total_active, total_pieces;
+  const int tid = threadIdx.x;
+  const int per = (T + kGroupThreads - 1) / kGroupThreads;
+  const int b = min(T, tid * per), e = min(T, b + per);
+  auto slot_at = [&](int t) {
+    const int s = slots[t];
+    return (s >= 0 && s < num_slots) ? s : -1;
+  };
+  const int before = b > 0 ? slot_at(b - 1) : -1;
+  int active = 0, last_run = -1, prev = before;
+  for (int t = b; t < e; ++t) {
+    const int s = slot_at(t);
+    if (s >= 0) {
+      ++active;
+      if (s != prev) last_run = t;
+    }
+    prev = s;
+  }
+  const int apos = block_exclusive_sum(active, wtmp, &total_active);  // active tokens before b
+  const int carry = block_exclusive_max(last_run, wtmp);              // last run start before b
+  int start = carry, pieces = 0;
+  prev = before;
+  for (int t = b; t < e; ++t) {
+    const int s = slot_at(t);
+    if (s >= 0) {
+      if (s != prev) start = t;
+      if (s != prev || (chunk > 0 && (t - start) % chunk == 0)) ++pieces;
+    }
+    prev = s;
+  }
+  int id = block_exclusive_sum(pieces, wtmp, &total_pieces);
+  int pos = apos, ipos = total_active + (b - apos);  // next active / inactive position
+  start = carry;
+  prev = before;
+  for (int t = b; t < e; ++t) {
+    const int s = slot_at(t);
+    if (s >= 0) {
+      if (s != prev) start = t;
+      if (s != prev || (chunk > 0 && (t - start) % chunk == 0)) {
+        indptr[id] = pos;
+        seg_slots[id] = s;
+        ++id;
+      }
+      perm[pos++] = t;
+    } else {
+      perm[ipos++] = t;
+    }
+    prev = s;
+  }
+  if (tid == 0) {
+    indptr[total_pieces] = total_active;
+    *seg_count = total_pieces;
+  }
+}
+
 // Shared memory: start[num_slots + 2] (bucket num_slots collects inactive tokens,
 // num_slots + 1 is a dummy for padding lanes), segbase[num_slots + 1], scan scratch,
 // and, when it fits, a cache of the tokens' bucket ids.
@@ -191,7 +257,7 @@ __global__ void __launch_bounds__(kGroupThreads)
 group_tokens_kernel(const int32_t* __restrict__ slots, int T, int num_slots, int chunk,
                     int32_t* __restrict__ indptr, int32_t* __restrict__ seg_slots,
                     int32_t* __restrict__ perm, int32_t* __restrict__ seg_count,
-                    int cache_tokens, int blocked, int runs) {
+                    int cache_tokens, int blocked) {
   extern __shared__ int smem[];
   int* start = smem;                       // num_slots + 2
   int* segbase = start + num_slots + 2;    // num_slots + 1
@@ -202,9 +268,6 @@ group_tokens_kernel(const int32_t* __restrict__ slots, int T, int num_slots, int
   // Blocked scatter: per-warp bucket counts [32][num_slots + 2] and per-token ranks [T].
   uint16_t* wcount = reinterpret_cast<uint16_t*>(cache + (cache_tokens ? T : 0));
   uint16_t* rank = wcount + kGroupWarps * (num_slots + 2);
-  // runs (blocked scatter only): cut_runs codes of the positions, after the ranks.
-  int* code = reinterpret_cast<int*>(smem) + ((reinterpret_cast<uint8_t*>(rank + T + 1) -
-                                               reinterpret_cast<uint8_t*>(smem) + 3) >> 2);
   const int tid = threadIdx.x;
 
   for (int s = tid; s < num_slots + 2; s += kGroupThreads) start[s] = 0;
@@ -242,7 +305,7 @@ group_tokens_kernel(const int32_t* __restrict__ slots, int T, int num_slots, int
   block_exclusive_scan2(start, segbase, num_slots + 1, warp_a, warp_b, &totals[0], &totals[1]);
   const int n_active = start[num_slots];
   const int nseg = segbase[num_slots];
-  for (int s = tid; s < num_slots && !runs; s += kGroupThreads) {
+  for (int s = tid; s < num_slots; s += kGroupThreads) {
     const int begin = start[s];
     const int first = segbase[s];
     const int pieces = segbase[s + 1] - first;
@@ -251,7 +314,7 @@ group_tokens_kernel(const int32_t* __restrict__ slots, int T, int num_slots, int
       seg_slots[first + j] = s;
     }
   }
-  if (tid == 0 && !runs) {
+  if (tid == 0) {
     indptr[nseg] = n_active;
     *seg_count = nseg;
   }
@@ -298,17 +361,7 @@ group_tokens_kernel(const int32_t* __restrict__ slots, int T, int num_slots, int
     __syncthreads();
     for (int t = tid; t < T; t += kGroupThreads) {
       const int bucket = bucket_of(t);
-      const int pos = start[bucket] + wcount[(t / per) * nb + bucket] + rank[t];
-      perm[pos] = t;
-      // A run of the slot starts at pos when the token before t has another slot; the
-      // slot's range starts there when pos is its first position.
-      if (runs && bucket < num_slots)
-        code[code_at(pos)] = ((t == 0 || bucket_of(t - 1) != bucket) ? 1 : 0) |
-                    (pos == start[bucket] ? (bucket + 1) << 1 : 0);
-    }
-    if (runs) {
-      __syncthreads();
-      cut_runs(code, n_active, chunk, indptr, seg_slots, seg_count, warp_a, &totals[0]);
+      perm[start[bucket] + wcount[(t / per) * nb + bucket] + rank[t]] = t;
     }
     return;
   }
@@ -493,10 +546,10 @@ extern "C" int lf_split_runs(const int32_t*, const int32_t*, const int32_t*, con
 namespace lfb {
 namespace {
 // Launch plan of group_tokens_kernel for T tokens: shared bytes, token cache, blocked
-// scatter, and whether the run cut fits in the same launch.
+// scatter.
 struct GroupPlan {
   size_t bytes;
-  int cache, blocked, runs_fit;
+  int cache, blocked;
 };
 constexpr size_t kGroupSmemLimit = 200 * 1024;
 inline GroupPlan group_plan(int T, int num_slots) {
@@ -508,8 +561,6 @@ inline GroupPlan group_plan(int T, int num_slots) {
   const size_t blocked_extra = sizeof(uint16_t) * (size_t(kGroupWarps) * (num_slots + 2) + size_t(T) + 1);
   g.blocked = T >= 64 && T <= 65535 && g.bytes + blocked_extra + 16 <= kGroupSmemLimit ? 1 : 0;
   if (g.blocked) g.bytes += blocked_extra + 16;
-  // The run cut's codes: one int per token after the ranks (4-byte aligned).
-  g.runs_fit = g.blocked && g.cache && g.bytes + sizeof(int) * size_t(code_ints(T)) + 8 <= kGroupSmemLimit ? 1 : 0;
   return g;
 }
 
@@ -527,12 +578,11 @@ int check_group_args(const int32_t* slots, int64_t num_tokens, int32_t num_slots
 }
 
 int launch_group(const int32_t* slots, int T, int32_t num_slots, int32_t chunk, int32_t* indptr, int32_t* seg_slots,
-                 int32_t* perm, int32_t* count, const GroupPlan& g, int runs, cudaStream_t stream) {
+                 int32_t* perm, int32_t* count, const GroupPlan& g, cudaStream_t stream) {
   static int flags[64] = {};
   if (int rc = ensure_smem(group_tokens_kernel, int(kGroupSmemLimit), flags)) return rc;
-  const size_t bytes = g.bytes + (runs ? sizeof(int) * size_t(code_ints(T)) + 8 : 0);
-  group_tokens_kernel<<<1, kGroupThreads, bytes, stream>>>(slots, T, num_slots, chunk, indptr, seg_slots, perm,
-                                                          count, g.cache, g.blocked, runs);
+  group_tokens_kernel<<<1, kGroupThreads, g.bytes, stream>>>(slots, T, num_slots, chunk, indptr, seg_slots, perm,
+                                                            count, g.cache, g.blocked);
   return check_launch("group_tokens");
 }
 }  // namespace
@@ -548,32 +598,19 @@ extern "C" int lf_group_tokens(const int32_t* slots, int64_t num_tokens, int32_t
     return rc;
   const int T = static_cast<int>(num_tokens);
   return launch_group(slots, T, num_slots, chunk, segment_indptr, segment_slots, token_indices, segment_count,
-                      group_plan(T, num_slots), 0, static_cast<cudaStream_t>(stream));
+                      group_plan(T, num_slots), static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int lf_group_token_runs(const int32_t* slots, int64_t num_tokens, int32_t num_slots,
                                    int32_t chunk, int32_t* segment_indptr, int32_t* segment_slots,
-                                   int32_t* token_indices, int32_t* segment_count, int32_t* scratch,
-                                   void* stream) {
+                                   int32_t* token_indices, int32_t* segment_count, void* stream) {
   using namespace lfb;
   if (int rc = check_group_args(slots, num_tokens, num_slots, segment_indptr, segment_slots, token_indices,
                                 segment_count, "group_token_runs"))
     return rc;
-  const int T = static_cast<int>(num_tokens);
-  const GroupPlan g = group_plan(T, num_slots);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (g.runs_fit)
-    return launch_group(slots, T, num_slots, chunk, segment_indptr, segment_slots, token_indices, segment_count, g, 1,
-                        s);
-  // Too large for one launch: the slot-ordered grouping into the scratch tables, then
-  // the run cut into the caller's.
-  if (!scratch) return fail(LF_E_INVALID, "group_token_runs: this batch needs the scratch tables (2T + 2 ints)");
-  int32_t* sc_indptr = scratch;
-  int32_t* sc_slots = scratch + T + 1;
-  int32_t* sc_count = sc_slots + (T > 0 ? T : 1);
-  if (int rc = launch_group(slots, T, num_slots, chunk, sc_indptr, sc_slots, token_indices, sc_count, g, 0, s)) return rc;
-  return lf_split_runs(sc_indptr, sc_slots, token_indices, sc_count, num_tokens, chunk, segment_indptr,
-                       segment_slots, segment_count, stream);
+  token_runs_kernel<<<1, kGroupThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      slots, int(num_tokens), num_slots, chunk, segment_indptr, segment_slots, token_indices, segment_count);
+  return check_launch("group_token_runs");
 }
 
 extern "C" int lf_split_runs(const int32_t* segment_indptr, const int32_t* segment_slots,

@@ -40,11 +40,12 @@ def group_tokens(
 ) -> Routing:
     """Group tokens by ``slots`` (int32 [T], -1 = no adapter) into <= ``chunk`` token segments.
 
-    ``chunk <= 0`` gives one segment per active slot.  ``runs=True`` cuts every maximal
-    run of consecutive tokens of a slot separately (``lf_group_token_runs``), so no segment
-    spans a gap in token order: in a prefill batch every segment is then one run of a
-    request's tokens, which the prefill kernels move as 2-D tiles.  The products are the
-    same either way.  Writes into ``out`` when given (every buffer must have room for T
+    ``chunk <= 0`` gives one segment per active slot.  ``runs=True`` groups by runs
+    instead (``lf_group_token_runs``): every maximal stretch of consecutive tokens with one
+    slot is cut into segments of at most ``chunk`` tokens from its start, in token order,
+    and ``token_indices`` lists the active tokens in token order (then the others).  In a
+    prefill batch every segment is then one run of a request's tokens, which the prefill
+    kernels move as 2-D tiles.  The products are the same either way.  Writes into ``out`` when given (every buffer must have room for T
     tokens), else allocates.
     """
     import torch
@@ -75,9 +76,6 @@ def group_tokens(
     with torch.cuda.device(slots.device):
         stream = _native.stream_of(slots.device)
         if runs:
-            # One launch for most batches; larger ones stage the slot-ordered tables in
-            # the scratch vector before the run cut.
-            scratch = torch.empty(2 * T + 2, dtype=torch.int32, device=slots.device)
             _native.call(
                 "lf_group_token_runs",
                 slots.data_ptr(),
@@ -88,7 +86,6 @@ def group_tokens(
                 out.segment_slots.data_ptr(),
                 out.token_indices.data_ptr(),
                 out.segment_count.data_ptr(),
-                scratch.data_ptr(),
                 stream,
             )
         else:

@@ -139,17 +139,36 @@ def split_runs_reference(indptr, seg_slots, perm, chunk):
     return out_indptr, out_slots
 
 
+def runs_reference(slots_np, num_slots, chunk):
+    """Runs of consecutive tokens with one slot, in token order, cut every `chunk` tokens
+    from each run's start; active tokens in token order, then the others."""
+    active = [0 <= int(s) < num_slots for s in slots_np]
+    perm = [t for t, a in enumerate(active) if a] + [t for t, a in enumerate(active) if not a]
+    indptr, seg_slots, pos, prev, start = [], [], 0, -1, 0
+    for t, s in enumerate(slots_np):
+        s = int(s) if active[t] else -1
+        if s >= 0:
+            if s != prev:
+                start = t
+            if s != prev or (chunk > 0 and (t - start) % chunk == 0):
+                indptr.append(pos)
+                seg_slots.append(s)
+            pos += 1
+        prev = s
+    indptr.append(pos)
+    return indptr, seg_slots, perm
+
+
 def check_runs(slots_np, num_slots, chunk):
     slots = torch.tensor(slots_np, dtype=torch.int32, device="cuda")
     routing = group_tokens(slots, num_slots, chunk=chunk, runs=True)
     torch.cuda.synchronize()
-    indptr, seg_slots, perm, _ = ref.group_tokens(slots_np, num_slots, chunk)
-    want_indptr, want_slots = split_runs_reference(indptr, seg_slots, perm, chunk)
+    want_indptr, want_slots, want_perm = runs_reference(slots_np, num_slots, chunk)
     count = int(routing.segment_count.item())
     assert count == len(want_slots)
     assert routing.segment_indptr[: count + 1].tolist() == want_indptr
     assert routing.segment_slots[:count].tolist() == want_slots
-    assert routing.token_indices[: len(slots_np)].tolist() == perm.tolist()
+    assert routing.token_indices[: len(slots_np)].tolist() == want_perm
     # Every segment is one run of one slot, at most `chunk` tokens.
     ind = routing.segment_indptr[: count + 1].cpu().numpy()
     tok = routing.token_indices.cpu().numpy()
@@ -158,6 +177,28 @@ def check_runs(slots_np, num_slots, chunk):
         assert len(run) >= 1 and (chunk <= 0 or len(run) <= chunk)
         assert np.all(np.diff(run) == 1)
         assert np.all(slots_np[run] == routing.segment_slots[s].item())
+
+
+def check_split(slots_np, num_slots, chunk):
+    # lf_split_runs on the slot-ordered grouping: the same token_indices, segments cut at
+    # every gap in token order.
+    from loraforge_b200 import _native
+
+    T = len(slots_np)
+    slots = torch.tensor(slots_np, dtype=torch.int32, device="cuda")
+    first = group_tokens(slots, num_slots, chunk=chunk)
+    out = empty_routing(T, "cuda")
+    _native.call("lf_split_runs", first.segment_indptr.data_ptr(), first.segment_slots.data_ptr(),
+                 first.token_indices.data_ptr(), first.segment_count.data_ptr(), T, chunk,
+                 out.segment_indptr.data_ptr(), out.segment_slots.data_ptr(), out.segment_count.data_ptr(),
+                 _native.stream_of(slots.device))
+    torch.cuda.synchronize()
+    indptr, seg_slots, perm, _ = ref.group_tokens(slots_np, num_slots, chunk)
+    want_indptr, want_slots = split_runs_reference(indptr, seg_slots, perm, chunk)
+    count = int(out.segment_count.item())
+    assert count == len(want_slots)
+    assert out.segment_indptr[: count + 1].tolist() == want_indptr
+    assert out.segment_slots[:count].tolist() == want_slots
 
 
 @pytest.mark.parametrize("chunk", [0, 5, 16, 128])
@@ -169,15 +210,19 @@ def test_split_runs_prefill_batches(seed, chunk):
     lengths = np.maximum(1, rng.geometric(1 / 200, size=int(rng.integers(1, 60))))
     owners = rng.integers(-1, num_slots, size=len(lengths))
     check_runs(np.repeat(owners, lengths), num_slots, chunk)
+    check_split(np.repeat(owners, lengths), num_slots, chunk)
 
 
 @pytest.mark.parametrize("chunk", [0, 3, 16])
 def test_split_runs_scattered_and_edge_cases(chunk):
     rng = np.random.default_rng(7)
-    check_runs(rng.integers(-2, 9, size=5000), 8, chunk)  # decode-like: many one-token runs
-    check_runs(np.full(1, 3), 4, chunk)
-    check_runs(np.full(300, -1), 4, chunk)  # no active token: no segment
-    check_runs(np.arange(70) % 2, 2, chunk)  # every run one token long
-    # Past the one-launch form's 65535 tokens: grouping into the scratch tables, then the cut.
+    for check in (check_runs, check_split):
+        check(rng.integers(-2, 9, size=5000), 8, chunk)  # decode-like: many one-token runs
+        check(np.full(1, 3), 4, chunk)
+        check(np.full(300, -1), 4, chunk)  # no active token: no segment
+        check(np.arange(70) % 2, 2, chunk)  # every run one token long
+    # A batch past the split kernel's shared-memory codes (global-memory walks there).
     lengths = np.maximum(1, rng.geometric(1 / 900, size=90))
-    check_runs(np.repeat(rng.integers(-1, 12, size=len(lengths)), lengths)[:70000], 12, chunk)
+    big = np.repeat(rng.integers(-1, 12, size=len(lengths)), lengths)[:70000]
+    check_runs(big, 12, chunk)
+    check_split(big, 12, chunk)

@@ -44,7 +44,7 @@ def test_invalid_arguments_fail_before_any_device_work():
     with pytest.raises(RuntimeError, match="num_slots"):
         _native.call("lf_group_tokens", None, 4, 0, 16, None, None, None, None, None)
     with pytest.raises(RuntimeError, match="num_slots"):
-        _native.call("lf_group_token_runs", None, 4, 0, 16, None, None, None, None, None, None)
+        _native.call("lf_group_token_runs", None, 4, 0, 16, None, None, None, None, None)
     with pytest.raises(RuntimeError, match="must not alias"):
         _native.call("lf_split_runs", 8, 16, 24, 32, 4, 16, 8, 40, 48, None)
     with pytest.raises(RuntimeError, match="aligned"):
