@@ -95,6 +95,9 @@ struct Params {
   int stages, stage_bytes;  // of the kernel being launched
   int max_tokens;           // longer segments are left to the prefill (tcgen05) kernels
   CUtensorMap tmap_a;  // A as 2-D [slots*S*cap rows, K], boxes of 8 rows x min(kc, 256)
+  // The same with boxes of 64 / 32 / 16 rows: for kc <= 256 the 8-row groups of a stage are
+  // plain row-major, so fewer, taller boxes fill the same layout.
+  CUtensorMap tmap_a_rows[3];
 };
 
 // Producer -> consumer description of one stage (lives at the end of the stage).
@@ -328,7 +331,10 @@ __global__ void __launch_bounds__(kThreads, REGS ? 2 : 1)
     for (int i = tid; i < kSeg * p.rstride; i += kThreads) acc[i] = 0.f;
   // The A tensor map lives in kernel parameter space: fetch it while the preceding grid
   // finishes, so the first TMA issue does not wait for it.
-  if (tid == kConsumers) asm volatile("prefetch.tensormap [%0];" ::"l"(&p.tmap_a) : "memory");
+  if (tid == kConsumers) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&p.tmap_a) : "memory");
+    for (int h = 0; h < 3; ++h) asm volatile("prefetch.tensormap [%0];" ::"l"(&p.tmap_a_rows[h]) : "memory");
+  }
   __syncthreads();
   pdl_wait();  // x, metadata and the workspace may come from the preceding grid
   pdl_launch_dependents();
@@ -383,10 +389,26 @@ __global__ void __launch_bounds__(kThreads, REGS ? 2 : 1)
           bulk_g2s(st + lane * xpitch, p.x + int64_t(tok) * p.x_stride + k0, row_bytes, &full[stage]);
         const int row0 = si.g * p.S * p.cap;
         uint8_t* abase = st + kSeg * xpitch;
-        for (int i = lane; i < groups * boxes; i += 32) {
-          const int grp = i / boxes, box = i - grp * boxes;
-          tma_load_2d(abase + (grp * (p.kc / bw) + box) * (8 * bw * 2), &p.tmap_a, k0 + box * bw,
-                      row0 + grp * 8, &full[stage]);
+        if (p.kc <= 256) {
+          // One box per 64 / 32 / 16 / 8 rows of the groups' rows: a copy costs the copy
+          // engine about the same whatever its size up to a few KiB.
+          if (lane == 0)
+            for (int r0 = 0, left = groups * 8; left > 0;) {
+              const int h = left >= 64 ? 64 : left >= 32 ? 32 : left >= 16 ? 16 : 8;
+              const CUtensorMap* map = h == 64   ? &p.tmap_a_rows[0]
+                                       : h == 32 ? &p.tmap_a_rows[1]
+                                       : h == 16 ? &p.tmap_a_rows[2]
+                                                 : &p.tmap_a;
+              tma_load_2d(abase + r0 * bw * 2, map, k0, row0 + r0, &full[stage]);
+              r0 += h;
+              left -= h;
+            }
+        } else {
+          for (int i = lane; i < groups * boxes; i += 32) {
+            const int grp = i / boxes, box = i - grp * boxes;
+            tma_load_2d(abase + (grp * (p.kc / bw) + box) * (8 * bw * 2), &p.tmap_a, k0 + box * bw,
+                        row0 + grp * 8, &full[stage]);
+          }
         }
       }
     }
@@ -1197,10 +1219,15 @@ int fused_launch(const void* x, int64_t x_stride, const void* a, const void* b,
     const cuuint64_t strides[1] = {cuuint64_t(width) * 2};
     const cuuint32_t box[2] = {cuuint32_t(sc.kc < 256 ? sc.kc : 256), 8};
     const cuuint32_t estr[2] = {1, 1};
-    const CUresult r = encode(&p.tmap_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(a),
-                              dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = encode(&p.tmap_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(a), dims, strides, box,
+                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    for (int h = 0; h < 3 && r == CUDA_SUCCESS; ++h) {
+      const cuuint32_t tall[2] = {box[0], cuuint32_t(64 >> h)};
+      r = encode(&p.tmap_a_rows[h], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(a), dims, strides, tall,
+                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    }
     if (r != CUDA_SUCCESS) return fail(LF_E_CUDA, "fused_shrink_expand: cuTensorMapEncodeTiled failed");
   }
   int device = 0, sms = 0;
