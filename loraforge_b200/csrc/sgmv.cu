@@ -220,10 +220,13 @@ __device__ __forceinline__ void mma1688(float (&d)[4], uint32_t a0, uint32_t a1,
 // Stage layout: x rows (16 slots, pitch kc*2 + 64 bytes, one bulk copy per token), then
 // the A rows as 2-D TMA boxes of 8 rows x bw columns (bw = min(kc, 256)), box-major:
 // element (j, c) of the chunk at ((j/8)*(kc/bw) + c/bw) * 8*bw*2 + (j%8)*bw*2 + (c%bw)*2.
+// kc is a power of two of at least 64 (shrink_config), so bw is one too and the address
+// takes shifts and masks, not the integer divisions that would sit in front of every load.
 __device__ __forceinline__ const uint8_t* a_frag(const uint8_t* abase, int kc, int j, int kb, int t) {
-  const int bw = kc < 256 ? kc : 256;
+  const int lbw = kc < 256 ? 31 - __clz(kc) : 8;  // log2(bw)
   const int c = kb * 32;
-  return abase + ((j >> 3) * (kc / bw) + c / bw) * (8 * bw * 2) + (j & 7) * (bw * 2) + (c % bw) * 2 + 16 * t;
+  return abase + (((j >> 3) * (kc >> lbw) + (c >> lbw)) << (lbw + 4)) + ((j & 7) << (lbw + 1)) +
+         ((c & ((1 << lbw) - 1)) << 1) + 16 * t;
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int c0, int c1,
