@@ -811,34 +811,102 @@ __device__ __forceinline__ void expand_stage_pair(const Params& p, const ExpandH
   }
 }
 
-// First expand unit of part `part` of `parts` parts of equal estimated cost.  A unit
-// (segment s, 128 columns) costs kUnitCost + n_s, measured in units of one token row
-// (per-CTA timestamps of BASELINE config 1: a 512-column stage takes about 1.3 us plus
-// 0.013 us per token row), so the cost before segment s is
-// ncb * (kUnitCost * s + indptr[s] - indptr[0]): monotone in s, found by a 32-way search
-// of the warp (lanes probe evenly spaced segments, the ballot keeps the prefix).
+// Estimated cost of one expand unit (segment s, 128 columns) in units of one token row
+// (about 25 SM cycles): a base by the slot's B bucket plus one per token row.  Per-stage
+// clock64 counts on BASELINE configs 1 and 2 put a unit at about 470-630 cycles for
+// buckets up to 16 (stages of 512 columns), 780 for 32 (256 columns) and 1840 for 64 (128
+// columns, half the consumer warps idle), plus about 25 cycles per token row.
 constexpr int kUnitCost = 24;
-__device__ int expand_cost_split(const Params& p, int nseg, int ncb, int part, int parts, int lane) {
-  if (part <= 0 || nseg <= 0) return 0;
-  if (part >= parts) return nseg * ncb;
-  const int base = p.indptr[0];
-  auto before = [&](int s) { return int64_t(ncb) * (int64_t(kUnitCost) * s + (p.indptr[s] - base)); };
-  const int64_t target = before(nseg) * part / parts;
-  int lo = 0, hi = nseg;  // before(lo) <= target; the answer lies in [lo, hi]
-  while (lo < hi) {
-    const int step = (hi - lo + 31) / 32;
-    const int s = min(hi, lo + step * (lane + 1));
-    const unsigned le = __ballot_sync(0xffffffffu, before(s) <= target);
-    const int k = __popc(le);  // probes at or below the target (a prefix of the lanes)
-    const int next_lo = k > 0 ? min(hi, lo + step * k) : lo;
-    const int next_hi = k < 32 ? min(hi, lo + step * (k + 1) - 1) : hi;
-    lo = next_lo;
-    hi = max(lo, next_hi);
+__device__ __forceinline__ int expand_unit_cost(int bucket, int n) {
+  return (bucket <= 16 ? kUnitCost : bucket <= 32 ? 30 : 72) + n;
+}
+
+// Whole CTA (kThreads threads, before the warp roles split): this CTA's expand units
+// [bounds[0], bounds[1]).  Each thread sums the costs of a contiguous range of segments
+// (ncb units of expand_unit_cost each; a segment outside the contract costs as a bucket-16
+// one, its units are skipped by the producer), a block scan gives each range's start, and
+// the thread whose range holds a boundary (total * part / parts) places it inside its
+// segment.  When every segment has the same bucket and the CTAs get fewer than 32 units
+// each, the units split by count instead: a cost split would add a z reload at every
+// segment change to the light CTAs, which costs more than it balances (BASELINE config 1
+// qkv and down).  `ws` holds kThreads / 32 + 2 int64 values of shared memory.
+__device__ void expand_split(const Params& p, int nseg, int ncb, long long* ws, int* bounds) {
+  constexpr int kWarps = kThreads / 32;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int span = (nseg + kThreads - 1) / kThreads;
+  const int s0 = min(nseg, tid * span), s1 = min(nseg, s0 + span);
+  auto bucket_of = [&](int s) {
+    const int g = p.seg_slots[s];
+    return g >= 0 && g < p.num_slots ? p.b_strides[g] : 16;
+  };
+  auto unit_cost = [&](int s, int bucket) {
+    const int n = p.indptr[s + 1] - p.indptr[s];
+    return expand_unit_cost(bucket, n < 0 ? 0 : n > kSeg ? kSeg : n);
+  };
+  long long mine = 0;
+  int lo = 1 << 30, hi = -1;
+  for (int s = s0; s < s1; ++s) {
+    const int b = bucket_of(s);
+    lo = min(lo, b);
+    hi = max(hi, b);
+    mine += (long long)ncb * unit_cost(s, b);
   }
-  if (lo >= nseg) return nseg * ncb;
-  const int n = p.indptr[lo + 1] - p.indptr[lo];
-  const int64_t unit = (target - before(lo)) / (kUnitCost + max(0, n));
-  return lo * ncb + (unit < ncb ? int(unit) : ncb);
+  long long inc = mine;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const long long v = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += v;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+    hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+  }
+  if (tid == 0) {
+    ws[kWarps] = 1 << 30;  // min bucket
+    ws[kWarps + 1] = -1;   // max bucket
+  }
+  __syncthreads();
+  if (lane == 31) ws[warp] = inc;
+  if (lane == 0) {
+    atomicMin(&ws[kWarps], (long long)lo);
+    atomicMax(&ws[kWarps + 1], (long long)hi);
+  }
+  __syncthreads();
+  long long before = inc - mine, total = 0;
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) {
+    before += w < warp ? ws[w] : 0;
+    total += ws[w];
+  }
+  const int units = nseg * ncb;
+  const bool by_count = ws[kWarps] == ws[kWarps + 1] && units < 32 * int(gridDim.x);
+  for (int k = 0; k < 2; ++k) {
+    const int part = int(blockIdx.x) + k, parts = int(gridDim.x);
+    if (by_count) {
+      const int per = (units + parts - 1) / parts;
+      if (tid == 0) bounds[k] = min(units, part * per);
+      continue;
+    }
+    if (part <= 0 || part >= parts || total <= 0) {
+      if (tid == 0) bounds[k] = part <= 0 ? 0 : units;
+      continue;
+    }
+    const long long target = total * part / parts;  // < total: exactly one range holds it
+    if (before <= target && target < before + mine) {
+      long long acc = before;
+      for (int s = s0; s < s1; ++s) {
+        const int c = unit_cost(s, bucket_of(s));
+        if (target < acc + (long long)ncb * c) {
+          const long long unit = (target - acc) / c;
+          bounds[k] = s * ncb + (unit < ncb ? int(unit) : ncb);
+          break;
+        }
+        acc += (long long)ncb * c;
+      }
+    }
+  }
+  __syncthreads();
 }
 
 template <int MODE, bool STAGED>
@@ -864,22 +932,16 @@ __global__ void __launch_bounds__(kThreads, 2) sgmv_expand_kernel(const __grid_c
 
   const int nseg = segment_total(p);
   const int ncb = (p.N + kExpandCols - 1) / kExpandCols;
+  // The metadata read here comes from the grid before the shrink, which the shrink waited
+  // for (griddepcontrol.wait) before it let this grid launch.
+  __shared__ long long split_ws[kThreads / 32 + 2];
+  __shared__ int split_bounds[2];
+  expand_split(p, nseg, ncb, split_ws, split_bounds);
 
   if (warp == kConsumerWarps) {
     // ------------------------------------------------------------ producer warp
-    // B rows and y rows do not depend on the shrink: no griddepcontrol.wait here.  With at
-    // least 32 units per CTA (wide projections: a CTA's units stay within one or two
-    // segments) the units split the batch by estimated cost, not by count (a 16-token
-    // segment's stage costs about half again a 1-token one's: its y rows are copied too);
-    // narrower ones split by count, where the z reload at every segment change a cost
-    // split adds to the light CTAs outweighs the gain (BASELINE config 1 qkv and down).
-    const int total = nseg * ncb;
-    const bool by_cost = total >= 32 * int(gridDim.x);
-    const int per = (total + int(gridDim.x) - 1) / int(gridDim.x);
-    const int u0 = by_cost ? expand_cost_split(p, nseg, ncb, int(blockIdx.x), int(gridDim.x), lane)
-                           : min(total, int(blockIdx.x) * per);
-    const int u1 = by_cost ? expand_cost_split(p, nseg, ncb, int(blockIdx.x) + 1, int(gridDim.x), lane)
-                           : min(total, int(blockIdx.x) * per + per);
+    // B rows and y rows do not depend on the shrink: no griddepcontrol.wait here.
+    const int u0 = split_bounds[0], u1 = split_bounds[1];
     // Consecutive 256-column units of one segment are merged into a stage while its
     // B rows fit kBStage and its columns kStageCols.
     int cur = -1, tok = -1;
