@@ -48,6 +48,7 @@ METRIC = "multi-LoRA shrink+expand tokens/s"
 # call, from one ncu capture per (config, path, call); see profiles/ for the commands.
 TRAFFIC = {
     (1, "fused", "gate_up_proj.fused"): (19.430144 + 75.358720 + 3.842816) * 1e6,
+    (2, "fused", "proj.fused"): (51.121664 + 0.143360 + 49.703424 + 0.023040) * 1e6,
 }
 
 
