@@ -19,8 +19,10 @@
 //                        partials in chunk order into z[segment] and resets the counter.
 //                        The summation order depends only on the grid size, so results
 //                        are deterministic (no floating-point atomics).
-//   sgmv_expand_kernel   units (segment, 256-column block).  A stage holds the slot's
-//                        compact B rows of the block and the segment's y rows.  The
+//   sgmv_expand_kernel   units (segment, 128-column block), split over the CTAs by an
+//                        estimated cost that weighs the slot's B bucket (expand_split).
+//                        A stage holds the slot's compact B rows of one or more blocks
+//                        and the segment's y rows.  The
 //                        producer never waits for the shrink (B and y do not depend on
 //                        it), so the first stages are in flight while the shrink
 //                        finishes; consumers wait for it (griddepcontrol.wait) before
@@ -942,7 +944,7 @@ __global__ void __launch_bounds__(kThreads, 2) sgmv_expand_kernel(const __grid_c
     // ------------------------------------------------------------ producer warp
     // B rows and y rows do not depend on the shrink: no griddepcontrol.wait here.
     const int u0 = split_bounds[0], u1 = split_bounds[1];
-    // Consecutive 256-column units of one segment are merged into a stage while its
+    // Consecutive 128-column units of one segment are merged into a stage while its
     // B rows fit kBStage and its columns kStageCols.
     int cur = -1, tok = -1;
     Seg si{};
