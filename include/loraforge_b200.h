@@ -307,9 +307,8 @@ int64_t lf_fused_workspace_floats(int64_t num_tokens, int64_t width, int32_t num
  * (cudaGetSymbolAddress) with that device current; make that first call before any
  * stream capture.  All calls on a device share the buffer and it keeps the last call's
  * contents: the counters start zero-filled and every call leaves them at zero, so calls
- * of any sizes may follow one another; calls that overlap on the GPU (other streams,
- * or graphs replayed concurrently) race on the buffers and must be serialised by the
- * caller.
+ * of any sizes may follow one another; calls that overlap on the GPU (on other
+ * streams) race on the buffers and must be serialised by the caller.
  */
 int lf_fused_shrink_expand_noalloc(const void* x, int64_t x_stride, const void* a,
                                    const void* b, const int64_t* b_offsets,

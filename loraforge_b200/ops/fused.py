@@ -65,8 +65,9 @@ def lora_shrink_expand(
     one workspace serves any sequence of calls of the same sizes on one stream.
     ``workspace="builtin"`` uses the library's fixed per-device scratch instead
     (``lf_fused_shrink_expand_noalloc``: up to 16384 tokens, any sequence of sizes,
-    no allocation, so serving graphs of every batch size can share it); calls that
-    use it must not run concurrently on different streams of one device.
+    no allocation; the first call on a device should come before any stream
+    capture); calls that use it must not run concurrently on different streams of
+    one device.
     """
     _launch(
         "lf_fused_shrink_expand", _native.fused_workspace_floats, x, a, b, output, b_offsets,
