@@ -306,9 +306,13 @@ int64_t lf_fused_workspace_floats(int64_t num_tokens, int64_t width, int32_t num
  * The first call on a device looks up the buffer's device address
  * (cudaGetSymbolAddress) with that device current; make that first call before any
  * stream capture.  All calls on a device share the buffer and it keeps the last call's
- * contents: the counters start zero-filled and every call leaves them at zero, so calls
- * of any sizes may follow one another; calls that overlap on the GPU (on other
- * streams) race on the buffers and must be serialised by the caller.
+ * contents: the counters start zero-filled and every call leaves them at zero, also when
+ * a bounded device wait runs out (the kernel then still counts the work it gave up on;
+ * that call's output is invalid and lf_device_wait_timeouts reports it), so calls of any
+ * sizes may follow one another; lf_fused_noalloc_reset zeroes them explicitly.  Calls
+ * that overlap on the GPU (on other streams) race on the buffers and must be serialised
+ * by the caller.  The buffer addresses are looked up again after the device's context
+ * is destroyed and re-created (cudaDeviceReset).
  */
 int lf_fused_shrink_expand_noalloc(const void* x, int64_t x_stride, const void* a,
                                    const void* b, const int64_t* b_offsets,
@@ -320,6 +324,22 @@ int lf_fused_shrink_expand_noalloc(const void* x, int64_t x_stride, const void* 
                                    int64_t width, int32_t out_width, int32_t num_slices,
                                    int32_t capacity, int32_t num_slots, int32_t max_segments,
                                    int32_t numerics, void* stream);
+
+/*
+ * Zero the per-segment completion counters of the built-in scratch of
+ * lf_fused_shrink_expand_noalloc on the current device (cudaMemsetAsync on `stream`;
+ * allocates nothing).  No counterpart in the reference.
+ */
+int lf_fused_noalloc_reset(void* stream);
+
+/*
+ * Zero the completion counters of a caller-owned lf_fused_shrink_expand workspace of
+ * these sizes (cudaMemsetAsync on `stream`).  Every call leaves them at zero, also after
+ * an expired device wait; this restores a workspace whose contents were overwritten.
+ * No counterpart in the reference (its operators keep no workspace).
+ */
+int lf_fused_workspace_reset(float* workspace, int64_t workspace_floats, int64_t num_tokens,
+                             int64_t width, int32_t num_slices, int32_t capacity, void* stream);
 
 /*
  * Symmetric buffers and a one-shot sum over NVLink peer memory, for the row-parallel
@@ -336,8 +356,12 @@ int lf_fused_shrink_expand_noalloc(const void* x, int64_t x_stride, const void* 
  * own z (floats <= capacity_floats FP32 values, 16-byte aligned) in the same order on its
  * stream, and on return every rank's z holds the sum over ranks, added in rank order (the
  * same bits on every rank).  One launch of 16 CTAs; the epoch lives on the device, so the
- * call may be captured in a CUDA graph.  Waits for peers are bounded (well under 2 s); on
- * expiry z keeps this rank's partial and lf_peer_status reports 1.
+ * call may be captured in a CUDA graph.  Waits for peers are bounded: at most spin_limit
+ * polls of the flag (spin_limit <= 0 or above the default: the default of 2^22 polls, well
+ * under 2 s); on expiry z keeps this rank's partial and lf_peer_status reports 1.  A peer
+ * that arrives after this rank gave up still computes the full sum, so the ranks' z then
+ * differ: callers check lf_peer_status (a synchronising read) at a step boundary and
+ * discard the step's outputs when it is 1.
  */
 int64_t lf_peer_buffer_bytes(int64_t capacity_floats);
 int lf_peer_handle_bytes(void);
@@ -347,7 +371,7 @@ int lf_peer_close(void* buffer);
 int lf_peer_free(void* buffer);
 int lf_peer_status(void* own_buffer, int32_t* status, int32_t reset);
 int lf_peer_sum(const uint64_t* bases, int32_t rank, int32_t world, float* z, int64_t floats,
-                int64_t capacity_floats, void* stream);
+                int64_t capacity_floats, int64_t spin_limit, void* stream);
 
 /*
  * Number of bounded device-side waits (mbarrier polls in the bulk-copy kernels)

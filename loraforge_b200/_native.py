@@ -78,7 +78,9 @@ SIGNATURES = {
     "lf_peer_close": [_p],
     "lf_peer_free": [_p],
     "lf_peer_status": [_p, _p, _i32],
-    "lf_peer_sum": [_p, _i32, _i32, _p, _i64, _i64, _p],
+    "lf_peer_sum": [_p, _i32, _i32, _p, _i64, _i64, _i64, _p],
+    "lf_fused_workspace_reset": [_p, _i64, _i64, _i64, _i32, _i32, _p],
+    "lf_fused_noalloc_reset": [_p],
 }
 
 _lock = threading.Lock()

@@ -8,9 +8,11 @@
 //
 //   1. each of kPeerCtas CTAs copies its slice of the local partial into the rank's own
 //      buffer (slot = epoch & 1, double-buffered across calls);
-//   2. it stores the epoch into its flag in every peer's buffer (st.release.sys, after a
-//      system-scope fence), then waits until every peer's flag for this CTA index in its
-//      own buffer has reached the epoch (ld.acquire.sys, bounded);
+//   2. after a CTA barrier over its copies, one thread per peer stores the epoch into the
+//      CTA's flag in that peer's buffer with st.release.sys (release is cumulative: the
+//      barrier orders the other threads' copies before it, so a peer that acquires the
+//      flag sees the whole slice), then waits until every peer's flag for this CTA index
+//      in its own buffer has reached the epoch (ld.acquire.sys, bounded);
 //   3. it sums the slice over the G peers' buffers in rank order (P2P loads over NVLink)
 //      into the local z rows, so every rank gets the same bits.
 //
@@ -49,7 +51,8 @@ __device__ __forceinline__ uint32_t load_acquire_sys(const uint32_t* p) {
 
 __global__ void __launch_bounds__(kPeerThreads) peer_sum_kernel(const uint64_t* __restrict__ bases,
                                                                 int rank, int world, float* z,
-                                                                int64_t floats, int64_t capacity) {
+                                                                int64_t floats, int64_t capacity,
+                                                                long long spin_limit) {
   __shared__ uint32_t epoch_s;
   __shared__ int ok_s;
   const int tid = threadIdx.x, cta = blockIdx.x;
@@ -82,7 +85,7 @@ __global__ void __launch_bounds__(kPeerThreads) peer_sum_kernel(const uint64_t* 
     const uint32_t* flag = reinterpret_cast<const uint32_t*>(own) + cta * kPeerMaxWorld + tid;
     long long it = 0;
     while (int32_t(load_acquire_sys(flag) - epoch) < 0) {
-      if (++it > kSpinLimit) {
+      if (++it > spin_limit) {
         ok_s = 0;
         atomicOr(reinterpret_cast<int*>(own + kStatusOffset), 1);
         break;
@@ -172,13 +175,14 @@ extern "C" int lf_peer_status(void* own_buffer, int32_t* status, int32_t reset) 
 }
 
 extern "C" int lf_peer_sum(const uint64_t* bases, int32_t rank, int32_t world, float* z, int64_t floats,
-                           int64_t capacity_floats, void* stream) {
+                           int64_t capacity_floats, int64_t spin_limit, void* stream) {
   if (world < 1 || world > kPeerMaxWorld || rank < 0 || rank >= world)
     return fail(LF_E_INVALID, "peer_sum: world must be 1..16 and rank in [0, world)");
   if (floats < 0 || floats > capacity_floats) return fail(LF_E_INVALID, "peer_sum: more floats than the buffer holds");
   if (!bases || (floats && !z)) return fail(LF_E_INVALID, "peer_sum: null pointer");
   if ((reinterpret_cast<uintptr_t>(z) & 15) != 0) return fail(LF_E_INVALID, "peer_sum: z must be 16-byte aligned");
+  const long long limit = spin_limit > 0 && spin_limit < kSpinLimit ? spin_limit : kSpinLimit;
   peer_sum_kernel<<<kPeerCtas, kPeerThreads, 0, static_cast<cudaStream_t>(stream)>>>(bases, rank, world, z, floats,
-                                                                                     capacity_floats);
+                                                                                     capacity_floats, limit);
   return check_launch("peer_sum");
 }

@@ -311,6 +311,21 @@ __device__ __forceinline__ void publish_run(const Params& p, int* flag, int tid,
   // consumer reaches after having read it here.
 }
 
+// After an expired wait the consumers leave their loop at unit u of segment `seg` with the
+// units [max(u0, seg * nchunks), u1) unpublished.  One thread counts them on their segments'
+// counters anyway, and the CTA that completes a count returns it to zero without writing z:
+// those segments' outputs are invalid (the expiry is counted in g_lf_wait_timeouts), but the
+// workspace's counters stay consistent, so the next call on the same workspace (or on the
+// library's built-in scratch) is correct again.
+__device__ __forceinline__ void abandon_runs(const Params& p, int seg, int u0, int u1) {
+  for (int s = seg; s * p.nchunks < u1; ++s) {
+    const int first = max(u0, s * p.nchunks), last = min(u1, (s + 1) * p.nchunks);
+    if (last <= first) continue;
+    const int old = atomicAdd(&p.counters[s], last - first);
+    if (old + (last - first) == p.nchunks) atomicExch(&p.counters[s], 0);
+  }
+}
+
 template <bool REGS>
 __global__ void __launch_bounds__(kThreads, REGS ? 2 : 1)
     sgmv_shrink_kernel(const __grid_constant__ Params p) {
@@ -450,7 +465,10 @@ __global__ void __launch_bounds__(kThreads, REGS ? 2 : 1)
         if (lane == 0) mbar_arrive(&empty[stage]);
       }
       if (!(u + 1 == u1 || chunk + 1 == p.nchunks)) continue;  // run continues
-      if (!consumers_all(!aborted)) break;
+      if (!consumers_all(!aborted)) {
+        if (tid == 0) abandon_runs(p, seg, u0, u1);
+        break;
+      }
       if (!ok) continue;
       float* rw = red + warp * kSeg * 8;  // [warp][16 rows][8 cols]
       *reinterpret_cast<float2*>(rw + g * 8 + 2 * t) = make_float2(d[0], d[1]);
@@ -471,7 +489,10 @@ __global__ void __launch_bounds__(kThreads, REGS ? 2 : 1)
     for (int u = u0; u < u1; ++u, ring.next(NS), chunk = chunk + 1 == p.nchunks ? (++seg, 0) : chunk + 1) {
       const int stage = ring.stage;
       const bool got = mbar_wait(&full[stage], ring.phase);
-      if (!consumers_all(got)) break;
+      if (!consumers_all(got)) {
+        if (tid == 0) abandon_runs(p, seg, u0, u1);
+        break;
+      }
       const uint8_t* st = smem + stage * SB;
       const Header h = *reinterpret_cast<const Header*>(st + hoff);
       if (h.ok) {
@@ -1361,9 +1382,61 @@ constexpr int64_t kNoAllocTokens = 16384;
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
 static __device__ __align__(256) int g_noalloc_counters[kNoAllocTokens];
 
+// Device addresses of the two arrays, per device index, with the context they were
+// looked up in: after a context is torn down and created again (cudaDeviceReset) the
+// module is loaded at new addresses, so an entry whose context is no longer current is
+// looked up again.
+struct NoAllocAddress {
+  void* context = nullptr;
+  float* scratch = nullptr;
+  int* counters = nullptr;
+};
 std::mutex g_noalloc_mutex;
-float* g_noalloc_address[64] = {};  // device address of the data buffer, per device
-int* g_noalloc_counters_address[64] = {};
+NoAllocAddress g_noalloc[64];
+
+using CtxGetCurrent = CUresult (*)(CUcontext*);
+CtxGetCurrent ctx_get_current() {
+  static CtxGetCurrent fn = nullptr;
+  static bool tried = false;
+  if (!tried) {  // called under g_noalloc_mutex
+    tried = true;
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult status;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &ptr, cudaEnableDefault, &status) == cudaSuccess &&
+        status == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrent>(ptr);
+  }
+  return fn;
+}
+
+// The built-in arrays' device addresses on the current device (looked up with it current).
+int noalloc_scratch(const char* what, Scratch* out) {
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess) return check_launch(what);
+  if (device < 0 || device >= 64) return fail(LF_E_UNSUPPORTED, "noalloc: device index above 63");
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  CtxGetCurrent get = ctx_get_current();
+  CUcontext ctx = nullptr;
+  if (get && get(&ctx) != CUDA_SUCCESS) ctx = nullptr;
+  NoAllocAddress& entry = g_noalloc[device];
+  if (!entry.scratch || !ctx || entry.context != static_cast<void*>(ctx)) {
+    // cudaGetSymbolAddress makes the device's primary context current if none is yet.
+    void* address = nullptr;
+    void* counters = nullptr;
+    cudaError_t err = cudaGetSymbolAddress(&address, g_noalloc_scratch);
+    if (err == cudaSuccess) err = cudaGetSymbolAddress(&counters, g_noalloc_counters);
+    if (err != cudaSuccess || !address || !counters) {
+      last_error() = std::string(what) + ": cudaGetSymbolAddress: " + cudaGetErrorString(err);
+      return LF_E_CUDA;
+    }
+    if (get && get(&ctx) != CUDA_SUCCESS) ctx = nullptr;
+    entry.context = ctx;
+    entry.scratch = static_cast<float*>(address);
+    entry.counters = static_cast<int*>(counters);
+  }
+  *out = Scratch{entry.scratch, entry.counters};
+  return LF_OK;
+}
 }  // namespace
 
 extern "C" int lf_fused_shrink_expand_noalloc(
@@ -1383,33 +1456,37 @@ extern "C" int lf_fused_shrink_expand_noalloc(
                    " tokens; use lf_fused_shrink_expand with a workspace";
     return LF_E_INVALID;
   }
-  int device = 0;
-  if (cudaGetDevice(&device) != cudaSuccess) return check_launch("fused_shrink_expand_noalloc");
-  if (device < 0 || device >= 64)
-    return fail(LF_E_UNSUPPORTED, "fused_shrink_expand_noalloc: device index above 63");
   Scratch scratch{};
-  {
-    // First call on a device: look up the buffers' device addresses with that device
-    // current.  The host-side names g_noalloc_scratch / g_noalloc_counters are not
-    // device addresses.
-    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-    if (!g_noalloc_address[device]) {
-      void* address = nullptr;
-      void* counters = nullptr;
-      cudaError_t err = cudaGetSymbolAddress(&address, g_noalloc_scratch);
-      if (err == cudaSuccess) err = cudaGetSymbolAddress(&counters, g_noalloc_counters);
-      if (err != cudaSuccess || !address || !counters) {
-        last_error() = std::string("fused_shrink_expand_noalloc: cudaGetSymbolAddress: ") +
-                       cudaGetErrorString(err);
-        return LF_E_CUDA;
-      }
-      g_noalloc_address[device] = static_cast<float*>(address);
-      g_noalloc_counters_address[device] = static_cast<int*>(counters);
-    }
-    scratch = Scratch{g_noalloc_address[device], g_noalloc_counters_address[device]};
-  }
+  if (int rc = noalloc_scratch("fused_shrink_expand_noalloc", &scratch)) return rc;
   return fused_launch(x, x_stride, a, b, b_offsets, b_strides, y, y_stride, segment_indptr,
                       segment_slots, token_indices, ranks, scales, slice_offsets, segment_count,
                       scratch, num_tokens, width, out_width, num_slices, capacity, num_slots,
                       max_segments, numerics, kSeg, stream, kPhaseShrink | kPhaseExpand);
+}
+
+// Zero the completion counters of the library's built-in scratch on the current device
+// (cudaMemsetAsync on the stream; allocates nothing).
+extern "C" int lf_fused_noalloc_reset(void* stream) {
+  Scratch scratch{};
+  if (int rc = noalloc_scratch("fused_noalloc_reset", &scratch)) return rc;
+  if (cudaMemsetAsync(scratch.counters, 0, sizeof(int) * kNoAllocTokens,
+                      static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return check_launch("fused_noalloc_reset");
+  return LF_OK;
+}
+
+// Zero the completion counters of a caller-owned decode workspace (cudaMemsetAsync).
+extern "C" int lf_fused_workspace_reset(float* workspace, int64_t workspace_floats, int64_t num_tokens,
+                                        int64_t width, int32_t num_slices, int32_t capacity,
+                                        void* stream) {
+  const int64_t need = lf_fused_workspace_floats(num_tokens, width, num_slices, capacity);
+  if (need < 0) return fail(LF_E_INVALID, "fused_workspace_reset: invalid sizes");
+  if (!workspace || workspace_floats < need)
+    return fail(LF_E_INVALID, "fused_workspace_reset: workspace too small for these sizes");
+  const Scratch scratch = decode_scratch(workspace, num_tokens, width, num_slices, capacity);
+  const int64_t T = num_tokens > 0 ? num_tokens : 1;
+  if (cudaMemsetAsync(scratch.counters, 0, sizeof(int) * size_t(T),
+                      static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return check_launch("fused_workspace_reset");
+  return LF_OK;
 }

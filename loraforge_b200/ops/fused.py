@@ -76,6 +76,33 @@ def lora_shrink_expand(
     )
 
 
+def reset_workspace(workspace, tokens: int, width: int, num_slices: int, capacity: int) -> None:
+    """Zero the completion counters of a ``lora_shrink_expand`` workspace (on its stream).
+
+    Every call leaves them at zero, also after a bounded device wait ran out (the kernel
+    counts the units it gave up on); use this when a workspace's contents may have been
+    overwritten, before reusing it.  Asynchronous; allocates nothing.
+    """
+    import torch
+
+    need = workspace_floats(tokens, width, num_slices, capacity)
+    if not isinstance(workspace, torch.Tensor) or workspace.dtype != torch.float32 or workspace.numel() < need:
+        raise ValueError(f"workspace must be an FP32 tensor of >= {need} elements")
+    with torch.cuda.device(workspace.device):
+        _native.call("lf_fused_workspace_reset", workspace.data_ptr(), workspace.numel(), tokens, width,
+                     num_slices, capacity, _native.stream_of(workspace.device))
+
+
+def reset_builtin_workspace(device=None) -> None:
+    """Zero the counters of the library's built-in scratch (``workspace="builtin"``) on
+    ``device`` (default: the current device), on its current stream.  Allocates nothing."""
+    import torch
+
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(device):
+        _native.call("lf_fused_noalloc_reset", _native.stream_of(device))
+
+
 def prefill_workspace_floats(tokens: int, width: int, num_slices: int, capacity: int) -> int:
     """Elements of the FP32 workspace ``lora_shrink_expand_prefill`` needs for these sizes."""
     return _native.prefill_workspace_floats(tokens, width, num_slices, capacity)

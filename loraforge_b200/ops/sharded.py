@@ -84,7 +84,8 @@ def column_parallel(x, a, b_shard, y_shard, **meta) -> None:
     lora_shrink_expand(x, a, b_shard, y_shard, **meta)
 
 
-def row_parallel(x_shard, a_shard, b_shard, y_shard, *, workspace, group=None, peer=None, **meta) -> None:
+def row_parallel(x_shard, a_shard, b_shard, y_shard, *, workspace, group=None, peer=None,
+                 check_peer: bool = True, **meta) -> None:
     """Row-parallel LoRA: partial shrink, all-reduce of the FP32 z rows, sharded expand.
 
     ``x_shard`` / ``a_shard`` hold this rank's input columns, ``b_shard`` / ``y_shard``
@@ -93,7 +94,14 @@ def row_parallel(x_shard, a_shard, b_shard, y_shard, *, workspace, group=None, p
     rows over NVLink peer memory in one kernel; without it the group's all-reduce is used.
     With ``group`` None and no initialised process group this is the single-rank
     computation.
+
+    A peer sum whose wait for another rank ran out leaves this rank's partial z, so the
+    output is invalid.  With ``check_peer`` (default) the call reads the peer status after
+    launching the expand (a synchronising read, skipped while the stream is being
+    captured) and raises ``RuntimeError`` on expiry; pass ``check_peer=False`` in a hot
+    loop and call ``peer.raise_on_expiry()`` at step boundaries instead.
     """
+    import torch
     import torch.distributed as dist
 
     sgmv_shrink(x_shard, a_shard, b_shard, y_shard, workspace=workspace, **meta)
@@ -104,6 +112,8 @@ def row_parallel(x_shard, a_shard, b_shard, y_shard, *, workspace, group=None, p
     elif dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
         dist.all_reduce(z, op=dist.ReduceOp.SUM, group=group)
     sgmv_expand(x_shard, a_shard, b_shard, y_shard, workspace=workspace, **meta)
+    if peer is not None and check_peer and not torch.cuda.is_current_stream_capturing():
+        peer.raise_on_expiry()
 
 
 class PeerAllReduce:
@@ -118,10 +128,12 @@ class PeerAllReduce:
     Construction and ``close`` are collective (every rank, same order; construction
     allocates and maps, calls do not).  ``capacity`` is the largest tensor (in floats) it
     will sum.  Calls are asynchronous on the tensor device's current stream and may be
-    captured in a CUDA graph.  ``status()`` is 1 after a wait for a peer ran out.
+    captured in a CUDA graph.  ``status()`` is 1 after a wait for a peer ran out;
+    ``spin_limit`` bounds that wait in polls of the flag (None: the library default, well
+    under 2 s).
     """
 
-    def __init__(self, capacity: int, *, group=None, device=None):
+    def __init__(self, capacity: int, *, group=None, device=None, spin_limit: int | None = None):
         import ctypes
 
         import torch
@@ -134,7 +146,9 @@ class PeerAllReduce:
         self.rank = dist.get_rank(group) if distributed else 0
         if self.world > 16:
             raise ValueError("peer sums support up to 16 ranks")
-        self.capacity, self.group = capacity, group
+        if spin_limit is not None and (type(spin_limit) is not int or spin_limit < 1):
+            raise ValueError("spin_limit must be a positive integer")
+        self.capacity, self.group, self.spin_limit = capacity, group, spin_limit or 0
         self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         lib = _native.library()
         handle = (ctypes.c_char * lib.lf_peer_handle_bytes())()
@@ -168,7 +182,7 @@ class PeerAllReduce:
             raise ValueError(f"z must be 16-byte aligned with at most {self.capacity} elements")
         with torch.cuda.device(self.device):
             _native.call("lf_peer_sum", self.bases.data_ptr(), self.rank, self.world, z.data_ptr(), z.numel(),
-                         self.capacity, _native.stream_of(self.device))
+                         self.capacity, self.spin_limit, _native.stream_of(self.device))
 
     def status(self, reset: bool = False) -> int:
         """1 if a wait for a peer expired since the last reset (synchronous)."""
@@ -180,6 +194,14 @@ class PeerAllReduce:
         with torch.cuda.device(self.device):
             _native.call("lf_peer_status", self._own, ctypes.byref(value), 1 if reset else 0)
         return value.value
+
+    def raise_on_expiry(self) -> None:
+        """Raise RuntimeError (and clear the status) if a wait for a peer ran out."""
+        if self.status(reset=True):
+            raise RuntimeError(
+                "peer z sum: a wait for another rank expired; this rank's z kept its partial "
+                "sum and the step's outputs are invalid"
+            )
 
     def close(self) -> None:
         """Collective: wait for every rank's last sum, then unmap and free the buffers."""
