@@ -20,7 +20,7 @@ from __future__ import annotations
 
 from loraforge_b200 import _native
 from loraforge_b200.annotations import ExperimentalAPI
-from loraforge_b200.ops.lora_rows import _distinct_output, _tensor, _vector
+from loraforge_b200.ops._contract import output_is_distinct, tensor_arg, vector_arg
 
 NUMERICS = {"fp32": 0, "reference": 1}
 
@@ -153,27 +153,27 @@ def _launch(entry, sizer, x, a, b, output, b_offsets, b_strides, ranks, scales,
             num_slices, numerics, workspace):
     import torch
 
-    _tensor(x, "x", 2, torch.bfloat16)
-    _tensor(a, "a", 3, torch.bfloat16, x.device)
-    _tensor(b, "b", 1, torch.bfloat16, x.device)
-    _tensor(output, "output", 2, torch.bfloat16, x.device)
+    tensor_arg(x, "x", 2, torch.bfloat16)
+    tensor_arg(a, "a", 3, torch.bfloat16, x.device)
+    tensor_arg(b, "b", 1, torch.bfloat16, x.device)
+    tensor_arg(output, "output", 2, torch.bfloat16, x.device)
     if type(num_slices) is not int or not 1 <= num_slices <= 4:
         raise ValueError("num_slices must be in 1..4")
     if numerics not in NUMERICS:
         raise ValueError("numerics must be 'fp32' or 'reference'")
-    _vector(ranks, "ranks", torch.int32, x.device, a.shape[0])
+    vector_arg(ranks, "ranks", torch.int32, x.device, a.shape[0])
     nslots = ranks.numel()
     for tensor, name, dtype in (
         (b_offsets, "b_offsets", torch.int64),
         (b_strides, "b_strides", torch.int32),
         (scales, "scales", torch.float32),
     ):
-        _vector(tensor, name, dtype, x.device, nslots)
-    _vector(segment_slots, "segment_slots", torch.int32, x.device)
-    _vector(segment_indptr, "segment_indptr", torch.int32, x.device, segment_slots.numel() + 1)
-    _vector(token_indices, "token_indices", torch.int32, x.device)
-    _vector(slice_offsets, "slice_offsets", torch.int32, x.device, num_slices + 1)
-    _vector(segment_count, "segment_count", torch.int32, x.device, 1)
+        vector_arg(tensor, name, dtype, x.device, nslots)
+    vector_arg(segment_slots, "segment_slots", torch.int32, x.device)
+    vector_arg(segment_indptr, "segment_indptr", torch.int32, x.device, segment_slots.numel() + 1)
+    vector_arg(token_indices, "token_indices", torch.int32, x.device)
+    vector_arg(slice_offsets, "slice_offsets", torch.int32, x.device, num_slices + 1)
+    vector_arg(segment_count, "segment_count", torch.int32, x.device, 1)
     if (
         a.shape[1] % num_slices
         or a.shape[2] != x.shape[1]
@@ -195,7 +195,7 @@ def _launch(entry, sizer, x, a, b, output, b_offsets, b_strides, ranks, scales,
         raise ValueError("expected aligned A/B/x with width and row stride multiples of 8")
     if output.stride(1) != 1 or output.stride(0) % 4 or output.stride(0) < output.shape[1] or output.data_ptr() % 8:
         raise ValueError("output rows must be 8-byte aligned with a row stride multiple of 4")
-    _distinct_output(
+    output_is_distinct(
         output,
         (x, a, b, b_offsets, b_strides, ranks, scales, segment_indptr, segment_slots,
          token_indices, slice_offsets, segment_count),

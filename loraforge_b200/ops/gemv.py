@@ -1,12 +1,11 @@
-"""Decode BGMV on padded SGLang slot buffers, on the sm_100a C ABI.
+"""Padded-layout decode BGMV (SGLang's slot buffers) over the sm_100a C ABI.
 
-Drop-in for ``loraforge.ops.gemv`` (src/loraforge/ops/gemv.py:46-238): same
-signatures, validation and messages; FP32, FP16 and BF16 activations.  The shrink
-is the slot-major kernel (each adapter's A rows are streamed once per tile of up
-to eight same-adapter tokens, with FP32 accumulation and one rounding to the
-activation dtype); the expand rounds the scaled delta to the activation dtype
-before adding it to the base, as the reference does.  No device value is read on
-the host, so warmed calls can be captured in a CUDA graph.
+Keeps the surface of ``loraforge.ops.gemv`` (src/loraforge/ops/gemv.py:46-238): call
+signatures, the checks and their messages, FP32 / FP16 / BF16 activations.  Kernels:
+``lf_bgmv_shrink`` groups the tokens of a slot into tiles of up to eight so each adapter's
+A rows are read once per tile, accumulating in FP32; ``lf_bgmv_expand`` rounds the scaled
+delta to the activation dtype before the base add.  Device values are never read on the
+host, so warmed calls can be recorded into a CUDA graph.
 """
 
 from __future__ import annotations
@@ -49,11 +48,13 @@ def _index_bits(t):
 
 
 def lora_shrink(x, weights, ranks, token_map, num_slices: int = 1):
-    """Apply packed LoRA A to decode tokens, preserving the activation dtype.
+    """Return z = A[token_map[t]] @ x[t] for every token, in x's dtype (a new tensor).
 
-    A is [slots, slices*max_rank, input]; slices are packed with stride
-    rank[slot]. The caller guarantees valid device metadata: mappings in
-    [0, slots), ranks in [0, max_rank]; rank zero marks base-model tokens.
+    ``weights`` holds each slot's A as [slices * capacity, width] rows; within a slot of
+    rank r, slice s occupies rows s*r .. s*r + r - 1, and z's columns follow the same
+    packing (the rest of each z row stays zero).  Sums are FP32, rounded once.  The
+    device metadata is trusted, not read on the host: token_map values in [0, slots),
+    ranks in [0, capacity]; a slot of rank 0 stands for the base model (zero row).
     """
     import torch
 
@@ -91,12 +92,13 @@ def lora_shrink(x, weights, ranks, token_map, num_slices: int = 1):
 
 
 def lora_expand(x, weights, ranks, scales, token_map, offsets, max_slice_size: int, base=None):
-    """Apply padded LoRA B and add the scaled delta to the optional base in place.
+    """Add scale * B[token_map[t]] @ z[t] into ``base`` (or a zero tensor) and return it.
 
-    B is [slots, total_output, max_rank]; x has the packed shrink layout. Slice
-    offsets increase from zero to total_output and each slice is at most
-    max_slice_size wide. The scaled delta is rounded to the activation dtype
-    before the base addition.
+    ``weights`` is B as [slots, total_output, capacity]; ``x`` is the packed z of
+    ``lora_shrink``.  ``offsets`` (on the device) split the output columns into slices
+    that start at zero, increase, and are at most ``max_slice_size`` wide; slice s reads
+    z columns s*r .. s*r + r - 1.  The scaled delta is rounded to the activation dtype
+    first and then added to the base, as in the reference operator.
     """
     import torch
 

@@ -1,11 +1,11 @@
-"""BGMV for vLLM's padded per-slice slot layouts, on the sm_100a C ABI.
+"""BGMV over vLLM's per-slice padded slot tensors, on the sm_100a C ABI.
 
-Drop-in for ``loraforge.ops.vllm_gemv`` (src/loraforge/ops/vllm_gemv.py:49-159):
-same signatures, checks and messages, and no torch/vLLM import until a call.  The
-reference splits K with FP32 atomics (nondeterministic); here every output is a
-fixed-order sum inside one thread-block cluster, so repeated calls are bitwise
-identical.  Routes of -1 keep the zero intermediate and leave output rows
-untouched.
+Keeps the surface of ``loraforge.ops.vllm_gemv`` (src/loraforge/ops/vllm_gemv.py:49-159):
+signatures, checks and messages; torch is imported only when a call is made.  The
+reference's shrink splits K across programs that add with FP32 atomics, so its low bits
+vary run to run; here the K split is summed in a fixed order within one thread-block
+cluster, and repeated calls give identical bits.  A route of -1 gives a zero intermediate
+row and leaves the output row as it was.
 """
 
 from loraforge_b200 import _native
@@ -62,10 +62,10 @@ def _descriptors(weights):
     reason="Inference-only padded-slot GEMV; vLLM 0.26.0 layouts, FP32 intermediates, sm_100a CUDA."
 )
 def shrink(x, weights, out, routes, *, scale=1.0):
-    """Write FP32 out[slices, tokens, rank] = scale * A[route] @ x.
+    """out[s, t] = scale * A_s[routes[t]] @ x[t] in FP32, for every weight slice s.
 
-    A is [slots, rank, width] or [slots, 1, rank, width]. Base routes (-1)
-    produce zero.
+    Each slice's A is [slots, rank, width] or [slots, 1, rank, width]; ``out`` is
+    [slices, tokens, rank] FP32.  Tokens routed to -1 get zero rows.
     """
     import torch
 
@@ -111,10 +111,11 @@ def shrink(x, weights, out, routes, *, scale=1.0):
     reason="Inference-only padded-slot GEMV; tolerance-based native parity, not full-model acceptance."
 )
 def expand(v, weights, y, routes, *, offset=0, add=True):
-    """Apply B[route] @ v to output slices in place, with FP32 accumulation.
+    """y[t, slice s columns] (+)= B_s[routes[t]] @ v[s, t], summed in FP32, cast once.
 
-    The FP32 intermediate is kept until the single final cast. Base-route rows and
-    columns outside the slices remain unchanged, even for add=False.
+    Slice s writes the columns offset + (widths of the earlier slices) onward; with
+    ``add`` the old y is added before the one cast.  Tokens routed to -1 and columns
+    outside the slices keep their values, also with ``add=False``.
     """
     import torch
 

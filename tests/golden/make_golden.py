@@ -217,7 +217,9 @@ def known_answers():
 
 
 def main(argv):
-    root = Path(argv[1] if len(argv) > 1 else "/root/reference").resolve()
+    if len(argv) != 2:
+        raise SystemExit("usage: python tests/golden/make_golden.py <reference source tree>")
+    root = Path(argv[1]).resolve()
     sys.path.insert(0, str(root / "src"))
     row_cases(root)
     gemv_cases(root)

@@ -1,5 +1,5 @@
-"""Prefill SGMV (lf_sgmv_prefill: tcgen05 tiles for segments of 16..128 tokens, decode
-kernels for shorter ones) on the B200 against the CPU oracle and the decode path."""
+"""Prefill SGMV (lf_sgmv_prefill: every segment of 1..128 tokens on the tcgen05 tiles, short
+ones leaving tile rows idle) on the B200 against the CPU oracle and the decode path."""
 
 import numpy as np
 import pytest
