@@ -13,8 +13,9 @@ routes the same seeded batch and holds its shard of one seeded global weight set
 
 At N=1 the line also carries ``sub``: configs 1 (Llama-3-8B decode, 256 tokens, 128
 rank-16 adapters), 2 (retained-rank compact B, ranks U{4..64}) and 3 (8192-token prefill
-in geometric segments, rank 64) and the row-operator pair on config 1, each timed the
-same way with its own roofline, e2e, CPU baseline and output check.
+in geometric segments, rank 64), the row-operator pair on config 1, and the reference's own
+CUDA row kernels on config 1 (built for sm_100a into oracle/_ref: the bar on the same box),
+each timed the same way with its own roofline, e2e, CPU baseline and output check.
 
 ``value``   tokens/s of the step replayed as a CUDA graph with inputs resident in HBM
             (L2 flushed by a 256 MiB write before every timed step, outside the step's
@@ -335,6 +336,8 @@ def run_step(w, mark=None):
     ``w.path == "fused"``: lora_shrink_expand per projection (prefill configs:
     lora_shrink_expand_prefill over segments of up to 128 tokens on the tcgen05 tiles);
     ``"rows"``: row_shrink + row_expand per projection (the reference's operator pair);
+    ``"reference_cuda"``: the same pair run by the reference's own CUDA kernels, built for
+    sm_100a into oracle/_ref (a comparison bar on the same box, never this repository's path);
     tensor-parallel configs: gate/up column-parallel, down as shrink, sum of the z rows
     over the ranks, expand.  ``mark(label)``, when given, records a CUDA event that starts
     the interval named `label` (ended by the next mark or "end").
@@ -377,6 +380,13 @@ def run_step(w, mark=None):
         elif w.path == "fused":
             mark(f"{p.name}.fused")
             fused_op(x, p.a, p.b, p.y, **meta, num_slices=p.S, workspace=p.workspace)
+        elif w.path == "reference_cuda":
+            mark(f"{p.name}.shrink")
+            w.ref.shrink(x, p.a, p.z, w.slots, p.ranks, p.S, p.cap)
+            mark(f"{p.name}.expand")
+            w.ref.expand(p.z, p.b, p.b_offsets, p.b_strides, p.y, r.segment_indptr, r.segment_slots,
+                         r.token_indices, p.ranks, p.scales, p.slice_offsets, r.segment_count, p.N, p.cap,
+                         2 * w.sms, 256)
         else:
             mark(f"{p.name}.shrink")
             row_shrink(x, p.a, p.z, w.slots, p.ranks, num_slices=p.S, max_rank=p.cap)
@@ -387,6 +397,8 @@ def run_step(w, mark=None):
 
 def launches_per_step(w):
     """This library's kernels per step: grouping, two per projection, the peer z sum."""
+    if w.path == "reference_cuda":
+        return 1  # only the grouping is this library's
     peer = 1 if (w.peer is not None and any(p.role == "row" for p in w.projections)) else 0
     return 1 + 2 * len(w.projections) + peer
 
@@ -432,7 +444,7 @@ def check_outputs(w):
         gate["rel_l2"] = float(np.linalg.norm(got - expected) / max(np.linalg.norm(expected), 1e-30))
         worst = {"excess": max(worst["excess"], gate["excess"]), "raw": max(worst["raw"], gate["raw"]),
                  "exact": min(worst["exact"], gate["exact"]), "rel_l2": max(worst["rel_l2"], gate["rel_l2"])}
-    ok = worst["rel_l2"] < 0.005 if w.path == "rows" else worst["excess"] <= 1e-2
+    ok = worst["rel_l2"] < 0.005 if w.path in ("rows", "reference_cuda") else worst["excess"] <= 1e-2
     return ok, worst
 
 
@@ -698,6 +710,13 @@ def measure(config, args, world, rank, local, path="fused", sub=False):
     device = torch.device("cuda", local)
     host = HostWorkload(config, args.seed)
     w = Workload(host, device, rank, world, path)
+    if path == "reference_cuda":
+        from oracle.build_ref import load
+
+        w.ref = load("lf_ref_rows")
+        if w.ref is None:
+            return {"unavailable": "oracle/_ref not built (python oracle/build_ref.py)"}
+        w.sms = torch.cuda.get_device_properties(device).multi_processor_count
     if w.sharded and world > 1 and args.allreduce == "peer":
         from loraforge_b200.ops.fused import z_rows
         from loraforge_b200.ops.sharded import PeerAllReduce
@@ -709,7 +728,7 @@ def measure(config, args, world, rank, local, path="fused", sub=False):
         ok, gate = check_outputs(w)
         ok = reduce_over_ranks(1.0 if ok else 0.0, world, op="min") == 1.0
         record["check"] = {"result": "pass" if ok else "fail",
-                           "gate": ("relative L2 < 0.005 vs FP32 oracle" if path == "rows" else
+                           "gate": ("relative L2 < 0.005 vs FP32 oracle" if path in ("rows", "reference_cuda") else
                                     "max|out-ref| beyond BF16 rounding <= 1e-2 RMS vs FP32 oracle"),
                            "excess": reduce_over_ranks(gate["excess"], world),
                            "raw": reduce_over_ranks(gate["raw"], world),
@@ -774,8 +793,10 @@ def measure(config, args, world, rank, local, path="fused", sub=False):
         }
     if "down_proj.allreduce" in per_kernel:  # the z sum, timed on its own
         record["allreduce_us"] = reduce_over_ranks(per_kernel["down_proj.allreduce"], world) * 1e3
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.profile:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.profile and path != "reference_cuda":
         record["cpu_baseline"] = cpu_baseline(host, budget_s=8.0 if sub else 12.0)
+    if path == "reference_cuda":
+        record["impl"] = "reference CUDA kernels (src/loraforge/ops/csrc/lora_rows.cu, sm_100a, oracle/_ref)"
     if w.peer is not None:
         w.peer.close()
     del w, flush
@@ -812,7 +833,7 @@ def main(argv=None):
     result.update(head)
     if world == 1 and args.config == 4 and not args.no_sub and not args.profile:
         sub = {}
-        for config, path in ((1, "fused"), (2, "fused"), (3, "fused"), (1, "rows")):
+        for config, path in ((1, "fused"), (2, "fused"), (3, "fused"), (1, "rows"), (1, "reference_cuda")):
             rec = measure(config, args, world, rank, local, path, sub=True)
             sub[f"config{config}" + ("" if path == "fused" else f"_{path}")] = rec
         result["sub"] = sub
