@@ -254,6 +254,30 @@ int64_t lf_sgmv_prefill_workspace_floats(int64_t num_tokens, int64_t width, int3
                                          int32_t capacity);
 
 /*
+ * Base projection with the LoRA delta in the same GEMM: y = x . W^T + scale_g . B_g . (A_g . x)
+ * for every routed token, y written once (never read).  Replaces the base-then-delta pair of
+ * the reference: lora_expand(..., base=) in src/loraforge/ops/gemv.py:130-238 and the base
+ * output the fleet backend threads through (src/loraforge/integrations/_sglang_fleet.py:340-347).
+ * W is [out_width, width] BF16 (row stride w_stride); the other operands and the routing are
+ * those of lf_sgmv_prefill (segments of up to 128 tokens), FP32 numerics only.  Multi-slice
+ * outputs need every slice boundary on a multiple of 256 columns.  Runs the prefill shrink,
+ * per-token slots, per-tile slot lists and one persistent tcgen05 GEMM (128 x 256 tiles);
+ * `workspace` holds lf_lora_base_gemm_workspace_floats(...) floats.
+ */
+int lf_lora_base_gemm(const void* x, int64_t x_stride, const void* w, int64_t w_stride, const void* a,
+                      const void* b, const int64_t* b_offsets, const int32_t* b_strides, void* y,
+                      int64_t y_stride, const int32_t* segment_indptr, const int32_t* segment_slots,
+                      const int32_t* token_indices, const int32_t* ranks, const float* scales,
+                      const int32_t* slice_offsets, const int32_t* segment_count, float* workspace,
+                      int64_t workspace_floats, int64_t num_tokens, int64_t width, int32_t out_width,
+                      int32_t num_slices, int32_t capacity, int32_t num_slots, int32_t max_segments,
+                      void* stream);
+
+/* Workspace floats lf_lora_base_gemm needs for these sizes (-1 if invalid). */
+int64_t lf_lora_base_gemm_workspace_floats(int64_t num_tokens, int64_t width, int32_t num_slices,
+                                           int32_t capacity);
+
+/*
  * The two halves of lf_fused_shrink_expand (same arguments, same workspace): the shrink
  * leaves the FP32 z rows in the workspace, the expand reads them.  Between the two a
  * caller may combine z across devices, e.g. sum it over the ranks of a row-parallel

@@ -20,7 +20,8 @@ CSRC = PACKAGE / "csrc"
 INCLUDE = PACKAGE.parent / "include"
 LIBDIR = PACKAGE / "_lib"
 LIBRARY = LIBDIR / "liblfb200.so"
-SOURCES = ("capi.cu", "grouping.cu", "shrink.cu", "expand.cu", "sgmv.cu", "sgmv_prefill.cu", "peer.cu")
+SOURCES = ("capi.cu", "grouping.cu", "shrink.cu", "expand.cu", "sgmv.cu", "sgmv_prefill.cu", "base_gemm.cu",
+           "peer.cu")
 ARCH = ("-gencode", "arch=compute_100a,code=sm_100a")
 FLAGS = ("-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr")
 

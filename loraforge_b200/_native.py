@@ -80,6 +80,10 @@ SIGNATURES = {
     "lf_peer_status": [_p, _p, _i32],
     "lf_peer_sum": [_p, _i32, _i32, _p, _i64, _i64, _i64, _p],
     "lf_fused_workspace_reset": [_p, _i64, _i64, _i64, _i32, _i32, _p],
+    "lf_lora_base_gemm": [
+        _p, _i64, _p, _i64, _p, _p, _p, _p, _p, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _i64,
+        _i64, _i64, _i32, _i32, _i32, _i32, _i32, _p,
+    ],
     "lf_fused_noalloc_reset": [_p],
 }
 
@@ -90,8 +94,8 @@ _lib = None
 def exported_symbols() -> tuple[str, ...]:
     """Every symbol the header declares (checked by the CPU test suite)."""
     return ("lf_version", "lf_last_error_string", "lf_fused_workspace_floats",
-            "lf_sgmv_prefill_workspace_floats", "lf_peer_buffer_bytes", "lf_peer_handle_bytes",
-            *SIGNATURES)
+            "lf_sgmv_prefill_workspace_floats", "lf_lora_base_gemm_workspace_floats",
+            "lf_peer_buffer_bytes", "lf_peer_handle_bytes", *SIGNATURES)
 
 
 def library() -> ctypes.CDLL:
@@ -115,7 +119,8 @@ def library() -> ctypes.CDLL:
                 fn = getattr(lib, name)
                 fn.restype = ctypes.c_int
                 fn.argtypes = args
-            for sizer in ("lf_fused_workspace_floats", "lf_sgmv_prefill_workspace_floats"):
+            for sizer in ("lf_fused_workspace_floats", "lf_sgmv_prefill_workspace_floats",
+                          "lf_lora_base_gemm_workspace_floats"):
                 getattr(lib, sizer).restype = ctypes.c_int64
                 getattr(lib, sizer).argtypes = [_i64, _i64, _i32, _i32]
             lib.lf_peer_buffer_bytes.restype = ctypes.c_int64
@@ -148,6 +153,14 @@ def prefill_workspace_floats(num_tokens: int, width: int, num_slices: int, capac
     n = library().lf_sgmv_prefill_workspace_floats(num_tokens, width, num_slices, capacity)
     if n < 0:
         raise ValueError("invalid sizes for the prefill workspace")
+    return n
+
+
+def lora_base_gemm_workspace_floats(num_tokens: int, width: int, num_slices: int, capacity: int) -> int:
+    """FP32 workspace size of lf_lora_base_gemm for these sizes."""
+    n = library().lf_lora_base_gemm_workspace_floats(num_tokens, width, num_slices, capacity)
+    if n < 0:
+        raise ValueError("invalid sizes for the base GEMM workspace")
     return n
 
 

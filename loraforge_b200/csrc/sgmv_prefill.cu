@@ -990,6 +990,38 @@ __global__ void __launch_bounds__(kExpandThreads, 1) prefill_expand_kernel(const
   }
 }
 
+// ====================================================================== z rows by token
+// For the base GEMM with the LoRA delta in its mainloop (base_gemm.cu): z_tok[t][c] = the
+// shrink's K parts summed in part order (as the expand sums them) for every token of a
+// valid segment, c < rpad.  One CTA per segment; CTAs past the live count exit.
+__global__ void __launch_bounds__(256) prefill_z_gather_kernel(const __grid_constant__ PParams p, float* z_tok) {
+  pdl_wait();  // the partial rows come from the shrink grid
+  pdl_launch_dependents();
+  const int nseg = segment_total(p);
+  const int seg = blockIdx.x;
+  if (seg >= nseg) return;
+  const PSeg si = prefill_segment(p, seg);
+  if (!si.ok) return;
+  const KSplit ks = k_split(p, nseg);
+  const int64_t part_stride = int64_t(p.T) * p.rpad;
+  const int q = p.rpad >> 2;  // float4 per row
+  for (int i = threadIdx.x; i < si.n * q; i += blockDim.x) {
+    const int m = i / q, c = (i - m * q) * 4;
+    const int t = p.perm[si.pos0 + m];
+    if (t < 0 || t >= p.T) continue;
+    const float* src = p.partial + int64_t(si.pos0 + m) * p.rpad + c;
+    float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int pp = 0; pp < ks.parts; ++pp) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(src + pp * part_stride));
+      sum.x += v.x;
+      sum.y += v.y;
+      sum.z += v.z;
+      sum.w += v.w;
+    }
+    *reinterpret_cast<float4*>(z_tok + int64_t(t) * p.rpad + c) = sum;
+  }
+}
+
 // ====================================================================== host side
 struct PrefillLayout {
   int rpad, kparts;
@@ -1024,9 +1056,9 @@ inline PFN_cuTensorMapEncodeTiled_v12000 prefill_tensor_map_encoder() {
   return fn;
 }
 
-template <typename Kernel>
+template <typename Kernel, typename... Extra>
 int launch_pdl(Kernel kernel, int grid, int block, int smem, cudaStream_t stream, const PParams& p,
-               const char* what) {
+               const char* what, Extra... extra) {
   cudaLaunchConfig_t config = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -1037,7 +1069,7 @@ int launch_pdl(Kernel kernel, int grid, int block, int smem, cudaStream_t stream
   config.blockDim = dim3(block);
   config.dynamicSmemBytes = smem;
   config.stream = stream;
-  const cudaError_t err = cudaLaunchKernelEx(&config, kernel, p);
+  const cudaError_t err = cudaLaunchKernelEx(&config, kernel, p, extra...);
   if (err != cudaSuccess) {
     last_error() = std::string(what) + ": " + cudaGetErrorString(err);
     return LF_E_CUDA;
@@ -1071,14 +1103,15 @@ extern "C" int64_t lf_sgmv_prefill_workspace_floats(int64_t num_tokens, int64_t 
   return prefill_layout(num_tokens, width, num_slices, capacity).total;
 }
 
-extern "C" int lf_sgmv_prefill(
+namespace lfb {
+int prefill_launch(
     const void* x, int64_t x_stride, const void* a, const void* b, const int64_t* b_offsets,
     const int32_t* b_strides, void* y, int64_t y_stride, const int32_t* segment_indptr,
     const int32_t* segment_slots, const int32_t* token_indices, const int32_t* ranks,
     const float* scales, const int32_t* slice_offsets, const int32_t* segment_count,
     float* workspace, int64_t workspace_floats, int64_t num_tokens, int64_t width,
     int32_t out_width, int32_t num_slices, int32_t capacity, int32_t num_slots,
-    int32_t max_segments, int32_t numerics, void* stream) {
+    int32_t max_segments, int32_t numerics, void* stream, float* z_tok) {
   if (num_tokens < 0 || num_tokens >= (int64_t(1) << 31) || width < 1 || width >= (int64_t(1) << 31))
     return fail(LF_E_INVALID, "sgmv_prefill: invalid token count or width");
   if (out_width < 1 || num_slices < 1 || num_slices > kMaxSlices || capacity < 1 || num_slots < 1)
@@ -1160,6 +1193,8 @@ extern "C" int lf_sgmv_prefill(
     if (r != CUDA_SUCCESS) return fail(LF_E_CUDA, "sgmv_prefill: cuTensorMapEncodeTiled failed");
   }
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (z_tok && cudaMemsetAsync(z_tok, 0, sizeof(float) * size_t(T) * l.rpad, s) != cudaSuccess)
+    return check_launch("sgmv_prefill (z by token): cudaMemsetAsync");
   // Shrink (2 CTAs per SM), then expand (1 per SM), all segments on the tensor cores.
   {
     const int smem = kShrinkStages * (kXTileBytes + l.rpad * kRowBytes) + 1024 + 128;
@@ -1170,6 +1205,12 @@ extern "C" int lf_sgmv_prefill(
     if (int rc = launch_pdl(prefill_shrink_kernel, grid, kShrinkThreads, smem, s, p,
                             "sgmv_prefill (shrink)"))
       return rc;
+  }
+  if (z_tok) {
+    // Shrink only: the z rows by token for the fused base GEMM (zeroed first, so tokens
+    // outside every valid segment carry no LoRA term).
+    const int grid = int(seg_cap < 1 ? 1 : seg_cap);
+    return launch_pdl(prefill_z_gather_kernel, grid, 256, 0, s, p, "sgmv_prefill (z by token)", z_tok);
   }
   {
     // Tiles and the identity, then 24 barriers, TMEM slot, slice offsets and abort word
@@ -1183,4 +1224,19 @@ extern "C" int lf_sgmv_prefill(
     if (int rc = launch_pdl(kernel, grid, kExpandThreads, smem, s, p, "sgmv_prefill (expand)")) return rc;
   }
   return LF_OK;
+}
+}  // namespace lfb
+
+extern "C" int lf_sgmv_prefill(
+    const void* x, int64_t x_stride, const void* a, const void* b, const int64_t* b_offsets,
+    const int32_t* b_strides, void* y, int64_t y_stride, const int32_t* segment_indptr,
+    const int32_t* segment_slots, const int32_t* token_indices, const int32_t* ranks,
+    const float* scales, const int32_t* slice_offsets, const int32_t* segment_count,
+    float* workspace, int64_t workspace_floats, int64_t num_tokens, int64_t width,
+    int32_t out_width, int32_t num_slices, int32_t capacity, int32_t num_slots,
+    int32_t max_segments, int32_t numerics, void* stream) {
+  return prefill_launch(x, x_stride, a, b, b_offsets, b_strides, y, y_stride, segment_indptr, segment_slots,
+                        token_indices, ranks, scales, slice_offsets, segment_count, workspace, workspace_floats,
+                        num_tokens, width, out_width, num_slices, capacity, num_slots, max_segments, numerics,
+                        stream, nullptr);
 }

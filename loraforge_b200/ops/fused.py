@@ -153,53 +153,9 @@ def _launch(entry, sizer, x, a, b, output, b_offsets, b_strides, ranks, scales,
             num_slices, numerics, workspace):
     import torch
 
-    tensor_arg(x, "x", 2, torch.bfloat16)
-    tensor_arg(a, "a", 3, torch.bfloat16, x.device)
-    tensor_arg(b, "b", 1, torch.bfloat16, x.device)
-    tensor_arg(output, "output", 2, torch.bfloat16, x.device)
-    if type(num_slices) is not int or not 1 <= num_slices <= 4:
-        raise ValueError("num_slices must be in 1..4")
-    if numerics not in NUMERICS:
-        raise ValueError("numerics must be 'fp32' or 'reference'")
-    vector_arg(ranks, "ranks", torch.int32, x.device, a.shape[0])
+    _check_operands(x, a, b, output, b_offsets, b_strides, ranks, scales, segment_indptr, segment_slots,
+                    token_indices, slice_offsets, segment_count, num_slices, numerics)
     nslots = ranks.numel()
-    for tensor, name, dtype in (
-        (b_offsets, "b_offsets", torch.int64),
-        (b_strides, "b_strides", torch.int32),
-        (scales, "scales", torch.float32),
-    ):
-        vector_arg(tensor, name, dtype, x.device, nslots)
-    vector_arg(segment_slots, "segment_slots", torch.int32, x.device)
-    vector_arg(segment_indptr, "segment_indptr", torch.int32, x.device, segment_slots.numel() + 1)
-    vector_arg(token_indices, "token_indices", torch.int32, x.device)
-    vector_arg(slice_offsets, "slice_offsets", torch.int32, x.device, num_slices + 1)
-    vector_arg(segment_count, "segment_count", torch.int32, x.device, 1)
-    if (
-        a.shape[1] % num_slices
-        or a.shape[2] != x.shape[1]
-        or output.shape[0] != x.shape[0]
-        or output.shape[1] < 1
-    ):
-        raise ValueError("A/output shapes must agree with slices and tokens")
-    if (
-        x.shape[1] % 8
-        or x.stride(1) != 1
-        or x.stride(0) % 8
-        or x.stride(0) < x.shape[1]
-        or x.data_ptr() % 16
-        or not a.is_contiguous()
-        or a.data_ptr() % 16
-        or not b.is_contiguous()
-        or b.data_ptr() % 16
-    ):
-        raise ValueError("expected aligned A/B/x with width and row stride multiples of 8")
-    if output.stride(1) != 1 or output.stride(0) % 4 or output.stride(0) < output.shape[1] or output.data_ptr() % 8:
-        raise ValueError("output rows must be 8-byte aligned with a row stride multiple of 4")
-    output_is_distinct(
-        output,
-        (x, a, b, b_offsets, b_strides, ranks, scales, segment_indptr, segment_slots,
-         token_indices, slice_offsets, segment_count),
-    )
     capacity = a.shape[1] // num_slices
     if isinstance(workspace, str):
         if workspace != "builtin" or entry != "lf_fused_shrink_expand":
@@ -266,6 +222,60 @@ def _launch(entry, sizer, x, a, b, output, b_offsets, b_strides, ranks, scales,
         )
 
 
+def _check_operands(x, a, b, output, b_offsets, b_strides, ranks, scales, segment_indptr, segment_slots,
+                    token_indices, slice_offsets, segment_count, num_slices, numerics):
+    """Structural checks of the fused operators' operands and routing (no device reads)."""
+    import torch
+
+    tensor_arg(x, "x", 2, torch.bfloat16)
+    tensor_arg(a, "a", 3, torch.bfloat16, x.device)
+    tensor_arg(b, "b", 1, torch.bfloat16, x.device)
+    tensor_arg(output, "output", 2, torch.bfloat16, x.device)
+    if type(num_slices) is not int or not 1 <= num_slices <= 4:
+        raise ValueError("num_slices must be in 1..4")
+    if numerics not in NUMERICS:
+        raise ValueError("numerics must be 'fp32' or 'reference'")
+    vector_arg(ranks, "ranks", torch.int32, x.device, a.shape[0])
+    nslots = ranks.numel()
+    for tensor, name, dtype in (
+        (b_offsets, "b_offsets", torch.int64),
+        (b_strides, "b_strides", torch.int32),
+        (scales, "scales", torch.float32),
+    ):
+        vector_arg(tensor, name, dtype, x.device, nslots)
+    vector_arg(segment_slots, "segment_slots", torch.int32, x.device)
+    vector_arg(segment_indptr, "segment_indptr", torch.int32, x.device, segment_slots.numel() + 1)
+    vector_arg(token_indices, "token_indices", torch.int32, x.device)
+    vector_arg(slice_offsets, "slice_offsets", torch.int32, x.device, num_slices + 1)
+    vector_arg(segment_count, "segment_count", torch.int32, x.device, 1)
+    if (
+        a.shape[1] % num_slices
+        or a.shape[2] != x.shape[1]
+        or output.shape[0] != x.shape[0]
+        or output.shape[1] < 1
+    ):
+        raise ValueError("A/output shapes must agree with slices and tokens")
+    if (
+        x.shape[1] % 8
+        or x.stride(1) != 1
+        or x.stride(0) % 8
+        or x.stride(0) < x.shape[1]
+        or x.data_ptr() % 16
+        or not a.is_contiguous()
+        or a.data_ptr() % 16
+        or not b.is_contiguous()
+        or b.data_ptr() % 16
+    ):
+        raise ValueError("expected aligned A/B/x with width and row stride multiples of 8")
+    if output.stride(1) != 1 or output.stride(0) % 4 or output.stride(0) < output.shape[1] or output.data_ptr() % 8:
+        raise ValueError("output rows must be 8-byte aligned with a row stride multiple of 4")
+    output_is_distinct(
+        output,
+        (x, a, b, b_offsets, b_strides, ranks, scales, segment_indptr, segment_slots,
+         token_indices, slice_offsets, segment_count),
+    )
+
+
 def sgmv_shrink(x, a, b, output, *, workspace, **routing) -> None:
     """First half of ``lora_shrink_expand``: z = A_g @ x[t] into ``workspace``.
 
@@ -308,3 +318,81 @@ def _launch_routed(entry, x, a, b, output, workspace, routing):
         raise TypeError(f"expected keyword arguments {keys}")
     _launch(entry, _native.fused_workspace_floats, x, a, b, output, *(routing[k] for k in keys),
             num_slices, numerics, workspace)
+
+
+def base_gemm_workspace_floats(tokens: int, width: int, num_slices: int, capacity: int) -> int:
+    """Elements of the FP32 workspace ``lora_base_gemm`` needs for these sizes."""
+    return _native.lora_base_gemm_workspace_floats(tokens, width, num_slices, capacity)
+
+
+@ExperimentalAPI(reason="Base projection GEMM with the LoRA delta in its mainloop; sm_100a tcgen05, FP32 numerics.")
+def lora_base_gemm(
+    x,
+    weight,
+    a,
+    b,
+    output,
+    *,
+    b_offsets,
+    b_strides,
+    ranks,
+    scales,
+    segment_indptr,
+    segment_slots,
+    token_indices,
+    slice_offsets,
+    segment_count,
+    num_slices: int = 1,
+    slice_widths=None,
+    workspace=None,
+) -> None:
+    """``output = x @ weight.T + scale * B_g @ (A_g @ x[t])`` for every routed token, in one GEMM.
+
+    The reference computes the base projection and then adds the LoRA delta into it
+    (``lora_expand(..., base=)``, src/loraforge/ops/gemv.py:130-238), which reads and
+    writes the output once more.  Here the delta is extra K steps of the base GEMM's
+    accumulator, so ``output`` is written once and never read (its old contents are
+    ignored).  ``weight`` is the base projection [N, width] (BF16, unit column stride);
+    the LoRA operands and routing are those of ``lora_shrink_expand_prefill`` (route with
+    ``group_tokens(..., chunk=128, runs=True)``).  Multi-slice outputs need every slice
+    width to be a multiple of 256: pass ``slice_widths`` (host integers) or the offsets are
+    read back once.  ``workspace``: FP32, ``base_gemm_workspace_floats(...)`` elements
+    (allocated when omitted).
+    """
+    import torch
+
+    _check_operands(x, a, b, output, b_offsets, b_strides, ranks, scales, segment_indptr, segment_slots,
+                    token_indices, slice_offsets, segment_count, num_slices, "fp32")
+    tensor_arg(weight, "weight", 2, torch.bfloat16, x.device)
+    output_is_distinct(output, (weight,))
+    if weight.stride(1) != 1 or weight.stride(0) % 8 or weight.shape[1] != x.shape[1] or weight.data_ptr() % 16:
+        raise ValueError("weight must be [N, width] with unit column stride, 16-byte aligned rows")
+    if weight.shape[0] != output.shape[1]:
+        raise ValueError("weight rows must match the output width")
+    if output.stride(0) % 8 or output.data_ptr() % 16:
+        raise ValueError("output rows must be 16-byte aligned with a row stride multiple of 8")
+    if num_slices > 1:
+        widths = slice_widths
+        if widths is None:
+            bounds = slice_offsets.tolist()
+            widths = [hi - lo for lo, hi in zip(bounds, bounds[1:])]
+        if len(widths) != num_slices or any(w % 256 for w in widths[:-1]):
+            raise ValueError("multi-slice lora_base_gemm needs slice widths that are multiples of 256")
+    capacity = a.shape[1] // num_slices
+    need = base_gemm_workspace_floats(x.shape[0], x.shape[1], num_slices, capacity)
+    if workspace is None:
+        workspace = torch.zeros(need, dtype=torch.float32, device=x.device)
+    if (not isinstance(workspace, torch.Tensor) or workspace.dtype != torch.float32
+            or workspace.device != x.device or workspace.numel() < need or workspace.data_ptr() % 16):
+        raise ValueError(f"workspace must be a 16-byte aligned FP32 buffer of >= {need} elements on x's device")
+    if x.shape[0] == 0:
+        return
+    with torch.cuda.device(x.device):
+        _native.call(
+            "lf_lora_base_gemm", x.data_ptr(), x.stride(0), weight.data_ptr(), weight.stride(0), a.data_ptr(),
+            b.data_ptr(), b_offsets.data_ptr(), b_strides.data_ptr(), output.data_ptr(), output.stride(0),
+            segment_indptr.data_ptr(), segment_slots.data_ptr(), token_indices.data_ptr(), ranks.data_ptr(),
+            scales.data_ptr(), slice_offsets.data_ptr(), segment_count.data_ptr(), workspace.data_ptr(),
+            workspace.numel(), x.shape[0], x.shape[1], output.shape[1], num_slices, capacity, ranks.numel(),
+            segment_slots.numel(), _native.stream_of(x.device),
+        )
