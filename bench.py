@@ -15,7 +15,9 @@ At N=1 the line also carries ``sub``: configs 1 (Llama-3-8B decode, 256 tokens, 
 rank-16 adapters), 2 (retained-rank compact B, ranks U{4..64}) and 3 (8192-token prefill
 in geometric segments, rank 64), the row-operator pair on config 1, and the reference's own
 CUDA row kernels on config 1 (built for sm_100a into oracle/_ref: the bar on the same box),
-each timed the same way with its own roofline, e2e, CPU baseline and output check.
+and on config 3 the base projection with the LoRA delta in one GEMM (lora_base_gemm) next to
+cuBLAS's base GEMM followed by lora_shrink_expand_prefill, each timed the same way with its
+own roofline, e2e, CPU baseline and output check.
 
 ``value``   tokens/s of the step replayed as a CUDA graph with inputs resident in HBM
             (L2 flushed by a 256 MiB write before every timed step, outside the step's
@@ -68,7 +70,7 @@ def parse_args(argv=None):
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--config", type=int, choices=(1, 2, 3, 4), default=4)
     p.add_argument("--seed", type=int, default=1234)
-    p.add_argument("--path", choices=("fused", "rows"), default="fused")
+    p.add_argument("--path", choices=("fused", "rows", "base_gemm", "base_cublas"), default="fused")
     p.add_argument("--allreduce", choices=("peer", "nccl"), default="peer",
                    help="tensor-parallel z sum: one kernel over NVLink peer memory, or NCCL")
     p.add_argument("--no-sub", action="store_true", help="skip the config 1-3 sub-records")
@@ -310,9 +312,18 @@ class Workload:
             key = (p.host.K, *p.k_range)
             if key not in self.x:
                 self.x[key] = host.x[p.host.K][:, p.k_range[0] : p.k_range[1]].contiguous().to(device)
-        sizer = prefill_workspace_floats if self.prefill and path == "fused" else workspace_floats
+        sizer = prefill_workspace_floats if self.prefill and path in ("fused", "base_cublas") else workspace_floats
         for p in self.projections:
             p.workspace = torch.zeros(sizer(self.T, p.K, p.S, p.cap), dtype=torch.float32, device=device)
+        if path in ("base_gemm", "base_cublas"):
+            # The base projection W [N, K] the LoRA delta is added to (seeded on the device).
+            from loraforge_b200.ops.fused import base_gemm_workspace_floats
+
+            for p in self.projections:
+                p.w = torch.randn(p.N, p.K, generator=gen, device=device, dtype=torch.bfloat16)
+                p.w.mul_(p.K**-0.5)
+                p.gemm_ws = torch.zeros(base_gemm_workspace_floats(self.T, p.K, p.S, p.cap), dtype=torch.float32,
+                                        device=device)
         self.slots = torch.from_numpy(self.slots_np).to(device)
         self.routing = empty_routing(self.T, device)
         self.peer = None
@@ -344,6 +355,7 @@ def run_step(w, mark=None):
     """
     from loraforge_b200.ops import row_expand, row_shrink
     from loraforge_b200.ops.fused import (
+        lora_base_gemm,
         lora_shrink_expand,
         lora_shrink_expand_prefill,
         sgmv_expand,
@@ -353,7 +365,7 @@ def run_step(w, mark=None):
     from loraforge_b200.ops.grouping import group_tokens
 
     mark = mark or (lambda label: None)
-    prefill = w.prefill and w.path == "fused"
+    prefill = w.prefill and w.path in ("fused", "base_gemm", "base_cublas")
     fused_op = lora_shrink_expand_prefill if prefill else lora_shrink_expand
     r = group_tokens(w.slots, w.nslots, chunk=128 if prefill else 16, runs=prefill, out=w.routing)
     routing = dict(
@@ -380,6 +392,17 @@ def run_step(w, mark=None):
         elif w.path == "fused":
             mark(f"{p.name}.fused")
             fused_op(x, p.a, p.b, p.y, **meta, num_slices=p.S, workspace=p.workspace)
+        elif w.path == "base_gemm":
+            mark(f"{p.name}.gemm")
+            lora_base_gemm(x, p.w, p.a, p.b, p.y, **meta, num_slices=p.S, slice_widths=p.widths,
+                           workspace=p.gemm_ws)
+        elif w.path == "base_cublas":
+            import torch
+
+            mark(f"{p.name}.gemm")
+            torch.matmul(x, p.w.t(), out=p.y)
+            mark(f"{p.name}.fused")
+            lora_shrink_expand_prefill(x, p.a, p.b, p.y, **meta, num_slices=p.S, workspace=p.workspace)
         elif w.path == "reference_cuda":
             mark(f"{p.name}.shrink")
             w.ref.shrink(x, p.a, p.z, w.slots, p.ranks, p.S, p.cap)
@@ -439,6 +462,11 @@ def check_outputs(w):
     worst = {"excess": 0.0, "raw": 0.0, "exact": 1.0, "rel_l2": 0.0}
     for p in w.projections:
         expected = oracle_delta(w.host, p, w.host.x[p.host.K])
+        if w.path in ("base_gemm", "base_cublas"):  # plus the base projection, FP32 on the GPU
+            prev = torch.backends.cuda.matmul.allow_tf32
+            torch.backends.cuda.matmul.allow_tf32 = False
+            expected = expected + (w.x_of(p).float() @ p.w.float().t()).cpu().numpy()
+            torch.backends.cuda.matmul.allow_tf32 = prev
         got = p.y.float().cpu().numpy()
         gate = fp32_gate(got, expected)
         gate["rel_l2"] = float(np.linalg.norm(got - expected) / max(np.linalg.norm(expected), 1e-30))
@@ -524,6 +552,13 @@ def measured_peaks():
         data = json.loads(path.read_text())
         return float(data["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def measured_tensor_peak():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        return float(json.loads(path.read_text())["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
 
 
 def capture(w):
@@ -745,16 +780,21 @@ def measure(config, args, world, rank, local, path="fused", sub=False):
     tokens_per_step = (1 if w.sharded else world) * w.T
     value = tokens_per_step * steps / (total_ms / 1e3)
     peak, peak_kind = measured_peaks()
-    kernels = {k: v for k, v in per_kernel.items() if k.split(".")[1] in ("shrink", "expand", "fused")}
+    kernels = {k: v for k, v in per_kernel.items() if k.split(".")[1] in ("shrink", "expand", "fused", "gemm")}
     dominant = max(kernels, key=kernels.get)
     name, kind = dominant.split(".")
     p = next(p for p in w.projections if p.name == name)
-    alg = {
-        "shrink": p.shrink_bytes(w.touched, w.t_active),
-        "expand": p.expand_bytes(w.touched, w.t_active),
-        "fused": p.shrink_bytes(w.touched, w.t_active) + p.expand_bytes(w.touched, w.t_active),
-    }[kind]
-    achieved = alg / (per_kernel[dominant] * 1e-3) / 1e9
+    if kind == "gemm":  # the base projection GEMM: tensor-bound, FLOPs of base plus LoRA
+        alg = 2 * w.T * p.K * p.N + (p.flops(w.slots_np) if path == "base_gemm" else 0)
+        achieved = alg / (per_kernel[dominant] * 1e-3) / 1e12
+        peak, peak_kind = measured_tensor_peak()
+    else:
+        alg = {
+            "shrink": p.shrink_bytes(w.touched, w.t_active),
+            "expand": p.expand_bytes(w.touched, w.t_active),
+            "fused": p.shrink_bytes(w.touched, w.t_active) + p.expand_bytes(w.touched, w.t_active),
+        }[kind]
+        achieved = alg / (per_kernel[dominant] * 1e-3) / 1e9
     record.update({
         "value": value,
         "unit": "tokens/s",
@@ -767,14 +807,14 @@ def measure(config, args, world, rank, local, path="fused", sub=False):
         "flops_per_step": w.flops_per_step(),
         "kernel_ms": per_kernel,
         "roofline": {
-            "bound": "hbm",
+            "bound": "tensor" if kind == "gemm" else "hbm",
             "kernel": dominant,
             "achieved": achieved,
             "peak": peak,
-            "unit": "GB/s",
+            "unit": "TFLOP/s" if kind == "gemm" else "GB/s",
             "frac": achieved / peak,
-            "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
-            "alg_bytes": alg,
+            "peak_source": f"{peak_kind} (MEASURED_PEAKS.json {'bf16_tflops' if kind == 'gemm' else 'hbm_gbs'})",
+            "alg_flops" if kind == "gemm" else "alg_bytes": alg,
             "traffic": TRAFFIC.get((config, path, dominant)),
         },
         "gpu_launches": launches_per_step(w) * steps,
@@ -793,7 +833,8 @@ def measure(config, args, world, rank, local, path="fused", sub=False):
         }
     if "down_proj.allreduce" in per_kernel:  # the z sum, timed on its own
         record["allreduce_us"] = reduce_over_ranks(per_kernel["down_proj.allreduce"], world) * 1e3
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.profile and path != "reference_cuda":
+    if (rank == 0 and world == 1 and not args.no_cpu_baseline and not args.profile
+            and path not in ("reference_cuda", "base_gemm", "base_cublas")):
         record["cpu_baseline"] = cpu_baseline(host, budget_s=8.0 if sub else 12.0)
     if path == "reference_cuda":
         record["impl"] = "reference CUDA kernels (src/loraforge/ops/csrc/lora_rows.cu, sm_100a, oracle/_ref)"
@@ -833,7 +874,8 @@ def main(argv=None):
     result.update(head)
     if world == 1 and args.config == 4 and not args.no_sub and not args.profile:
         sub = {}
-        for config, path in ((1, "fused"), (2, "fused"), (3, "fused"), (1, "rows"), (1, "reference_cuda")):
+        for config, path in ((1, "fused"), (2, "fused"), (3, "fused"), (1, "rows"), (1, "reference_cuda"),
+                             (3, "base_gemm"), (3, "base_cublas")):
             rec = measure(config, args, world, rank, local, path, sub=True)
             sub[f"config{config}" + ("" if path == "fused" else f"_{path}")] = rec
         result["sub"] = sub
