@@ -119,7 +119,8 @@ int lf_row_shrink(const void* x, int64_t x_stride, const void* a, void* z,
  * Same arithmetic, in the same order, as src/loraforge/ops/csrc/lora_rows.cu:67-162
  * (`expand` at :188-209) and src/loraforge/ops/csrc/rowexpand.cu:33-86.
  * row_tile in {2,4,8,16} splits segments into sub-tiles (work split only).
- * `threads` in {128, 256}; `blocks` is the persistent grid size.
+ * `threads` in {128, 256}; `blocks` is the persistent grid size (0: as many CTAs as the
+ * SMs hold at once).  Each item covers 2 * threads output columns.
  */
 int lf_row_expand(const void* z, const void* b, const int64_t* b_offsets,
                   const int32_t* b_strides, void* y, int64_t y_stride,

@@ -5,9 +5,12 @@
 // k = 0..bucket-1 in order with fused multiply-adds, the scaled delta rounded to
 // BF16, added to the BF16 base and rounded again), so it is bit-identical to the
 // reference kernel on identical inputs.  Its work item is a (segment or row-tile
-// sub-segment, column block) pair of a persistent grid; each thread keeps its B row
-// in registers and walks the segment's <= 16 tokens, whose z values are staged in
-// shared memory as FP32.
+// sub-segment, block of 2 x blockDim.x columns) pair of a persistent grid.  The
+// reference walks an item's tokens with one read-modify-write of y after another,
+// each a full memory round trip; here a thread keeps the B rows of its two columns
+// in registers as packed BF16 and loads the old y values of every token of the item
+// before the first product, so an item costs one round trip for all its tokens.
+// The sub-tile's z values are staged in shared memory as FP32.
 //
 // bgmv_expand_kernel and vllm_expand_kernel serve the padded SGLang and vLLM
 // layouts for FP32/FP16/BF16 activations.
@@ -18,64 +21,195 @@ namespace {
 
 constexpr int kMaxSlices = 4;
 constexpr int kSegRows = 16;
+constexpr int kColsPerThread = 2;  // output columns per thread and item
+
+// B row n of an item's slot held as packed BF16 pairs; the FP32 value of element k is
+// recovered at the multiply (bits << 16 is exact).
+template <int BR>
+struct BRow {
+  static constexpr int kWords = BR >= 2 ? BR / 2 : 1;
+  uint32_t w[kWords];
+
+  __device__ __forceinline__ void load(const uint16_t* bp) {
+    if constexpr (BR >= 8) {
+#pragma unroll
+      for (int q = 0; q < BR / 8; ++q) {
+        const uint4 v = reinterpret_cast<const uint4*>(bp)[q];
+        w[4 * q] = v.x;
+        w[4 * q + 1] = v.y;
+        w[4 * q + 2] = v.z;
+        w[4 * q + 3] = v.w;
+      }
+    } else if constexpr (BR == 4) {
+      const uint2 v = *reinterpret_cast<const uint2*>(bp);
+      w[0] = v.x;
+      w[1] = v.y;
+    } else if constexpr (BR == 2) {
+      w[0] = *reinterpret_cast<const uint32_t*>(bp);
+    } else {
+      w[0] = bp[0];
+    }
+  }
+  __device__ __forceinline__ float at(int k) const {
+    if constexpr (BR == 1) return __uint_as_float(w[0] << 16);
+    return (k & 1) ? __uint_as_float(w[k >> 1] & 0xffff0000u) : __uint_as_float(w[k >> 1] << 16);
+  }
+};
+
+// The reference's per-element arithmetic for one (token, column): FP32 fused
+// multiply-adds over k = 0..BR-1 in order from zero, the scaled sum rounded to BF16,
+// added to the old BF16 value and rounded again.  Rows of up to 16 elements are held
+// in registers (`head`); longer rows continue the same chain with 16-element chunks
+// read again from L1 for every token, which keeps the register count of the kernel
+// at the 16-element case.
+constexpr int kHeld = 16;
 
 template <int BR>
-__device__ __forceinline__ void load_b_row(const uint16_t* bp, float* b) {
-  if constexpr (BR >= 8) {
+__device__ __forceinline__ uint16_t expand_value(const float* zt, const uint16_t* brow,
+                                                 const BRow<(BR < kHeld ? BR : kHeld)>& head,
+                                                 float scale, uint32_t old) {
+  constexpr int H = BR < kHeld ? BR : kHeld;
+  float acc = 0.f;
 #pragma unroll
-    for (int q = 0; q < BR; q += 8) unpack_bf16x8(*reinterpret_cast<const uint4*>(bp + q), b + q);
-  } else if constexpr (BR == 4) {
-    const uint2 v = *reinterpret_cast<const uint2*>(bp);
-    b[0] = __uint_as_float(v.x << 16);
-    b[1] = __uint_as_float(v.x & 0xffff0000u);
-    b[2] = __uint_as_float(v.y << 16);
-    b[3] = __uint_as_float(v.y & 0xffff0000u);
-  } else if constexpr (BR == 2) {
-    const uint32_t v = *reinterpret_cast<const uint32_t*>(bp);
-    b[0] = __uint_as_float(v << 16);
-    b[1] = __uint_as_float(v & 0xffff0000u);
-  } else {
-    b[0] = bf16_bits_to_float(bp[0]);
+  for (int k = 0; k < H; ++k) acc = fmaf(zt[k], head.at(k), acc);
+#pragma unroll 1
+  for (int q = 1; q < BR / H; ++q) {
+    BRow<H> b;
+    b.load(brow + q * H);
+#pragma unroll
+    for (int k = 0; k < H; ++k) acc = fmaf(zt[q * H + k], b.at(k), acc);
   }
+  const float delta = round_through_bf16(acc * scale);
+  return uint16_t(float_to_bf16_bits(bf16_bits_to_float(old) + delta));
 }
 
-// One output column n for the tokens of the current item.
-template <int BR>
-__device__ __forceinline__ void expand_column(const uint16_t* bp, uint16_t* y, int64_t y_stride,
-                                              int n, int slice, int T, const int* rows,
-                                              const float* zs, float scale) {
-  float b[BR];
-  load_b_row<BR>(bp + int64_t(n) * BR, b);
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(smem))),
+               "l"(gmem)
+               : "memory");
+}
+
+// One item (sub-tile of T <= 16 rows, 2 * blockDim.x columns) for one thread, which
+// owns two columns c0, c1.  PAIRED (even row stride, 4-byte aligned output): the
+// columns are adjacent and one 4-byte value holds both.  Otherwise they are
+// blockDim.x apart and move as 2-byte values.
+//
+// Before the barrier that publishes the z values, the thread issues its B rows (into
+// registers) and, PAIRED, one asynchronous 4-byte copy per row of the old y values
+// into its own shared-memory column `ys` (token t at ys[t * pitch]), so the HBM round
+// trips of B, old y and z overlap.  A row listed twice in one item (malformed
+// routing) voids the snapshot: the item is then updated in token order with one
+// read-modify-write after another, as the reference's loop does.
+template <int BR, bool PAIRED>
+__device__ __noinline__ void expand_item(const uint16_t* __restrict__ z, const uint16_t* __restrict__ bslot,
+                                            uint16_t* y, int64_t y_stride, int base, int N,
+                                            const int* offs, int S, int cap, int rank, int T,
+                                            const int* rows, float* zs, float scale, uint32_t* ys) {
+  constexpr int H = BR < kHeld ? BR : kHeld;
+  const int tid = threadIdx.x, pitch = blockDim.x;
+  const int c0 = PAIRED ? base + 2 * tid : base + tid;
+  const int c1 = PAIRED ? c0 + 1 : c0 + pitch;
+  const bool one = c0 < N, two = c1 < N;
+  const uint16_t* brow0 = bslot + int64_t(c0) * BR;
+  const uint16_t* brow1 = bslot + int64_t(c1) * BR;
+  BRow<H> b0, b1;
+  if (one) b0.load(brow0);
+  if (two) b1.load(brow1);
+  if (PAIRED && two) {
+#pragma unroll
+    for (int t = 0; t < kSegRows; ++t)
+      if (t < T) cp_async4(ys + t * pitch, y + int64_t(rows[t]) * y_stride + c0);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
+  bool dup = false;
+  if (tid < T)
+    for (int u = 0; u < tid; ++u) dup |= rows[u] == rows[tid];
+  for (int i = tid; i < T * S * BR; i += pitch) {
+    const int t = i / (S * BR);
+    const int rem = i - t * S * BR;
+    const int s = rem / BR;
+    const int k = rem - s * BR;
+    zs[(t * kMaxSlices + s) * 64 + k] =
+        k < rank ? bf16_bits_to_float(z[int64_t(rows[t]) * S * cap + s * rank + k]) : 0.f;
+  }
+  const bool distinct = !__syncthreads_or(dup);
+  if (PAIRED && two) asm volatile("cp.async.wait_group 0;" ::: "memory");
+  if (!one) return;
+  int s0 = 0, s1 = 0;
+  for (int i = 1; i < S; ++i) {
+    if (c0 >= offs[i]) s0 = i;
+    if (c1 >= offs[i]) s1 = i;
+  }
+  if (!distinct) {
+    for (int t = 0; t < T; ++t) {
+      uint16_t* yp = y + int64_t(rows[t]) * y_stride;
+      const float* zt = zs + t * kMaxSlices * 64;
+      yp[c0] = expand_value<BR>(zt + s0 * 64, brow0, b0, scale, yp[c0]);
+      if (two) yp[c1] = expand_value<BR>(zt + s1 * 64, brow1, b1, scale, yp[c1]);
+    }
+    return;
+  }
+  if (!(PAIRED && two)) {  // 2-byte columns: both columns' old values, 8 rows at a time
+    uint16_t* ys16 = reinterpret_cast<uint16_t*>(ys);
+#pragma unroll 1
+    for (int t0 = 0; t0 < T; t0 += 8) {
+      uint16_t o0[8], o1[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint16_t* yp = y + int64_t(rows[min(t0 + j, T - 1)]) * y_stride;
+        o0[j] = yp[c0];
+        o1[j] = two ? yp[c1] : 0;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        ys16[2 * (t0 + j) * pitch] = o0[j];
+        ys16[2 * (t0 + j) * pitch + 1] = o1[j];
+      }
+    }
+  }
+#pragma unroll 1
   for (int t = 0; t < T; ++t) {
-    const float* zt = zs + (t * kMaxSlices + slice) * 64;
-    float acc = 0.f;
-#pragma unroll
-    for (int k = 0; k < BR; ++k) acc = fmaf(zt[k], b[k], acc);
-    uint16_t* yp = y + int64_t(rows[t]) * y_stride + n;
-    const float delta = bf16_bits_to_float(float_to_bf16_bits(acc * scale));
-    *yp = uint16_t(float_to_bf16_bits(bf16_bits_to_float(*yp) + delta));
+    const uint32_t w = ys[t * pitch];
+    const float* zt = zs + t * kMaxSlices * 64;
+    uint16_t* yp = y + int64_t(rows[t]) * y_stride;
+    const uint16_t v0 = expand_value<BR>(zt + s0 * 64, brow0, b0, scale, w & 0xffffu);
+    if (!two) {
+      yp[c0] = v0;
+      continue;
+    }
+    const uint16_t v1 = expand_value<BR>(zt + s1 * 64, brow1, b1, scale, w >> 16);
+    if (PAIRED) {
+      *reinterpret_cast<uint32_t*>(yp + c0) = uint32_t(v0) | (uint32_t(v1) << 16);
+    } else {
+      yp[c0] = v0;
+      yp[c1] = v1;
+    }
   }
 }
 
-__global__ void row_expand_kernel(const uint16_t* __restrict__ z, const uint16_t* __restrict__ B,
-                                  const int64_t* __restrict__ b_offsets,
-                                  const int32_t* __restrict__ b_strides, uint16_t* y,
-                                  int64_t y_stride, const int32_t* __restrict__ indptr,
-                                  const int32_t* __restrict__ seg_slots,
-                                  const int32_t* __restrict__ perm,
-                                  const int32_t* __restrict__ ranks,
-                                  const float* __restrict__ scales,
-                                  const int32_t* __restrict__ slice_offsets,
-                                  const int32_t* __restrict__ seg_count, int T_tokens, int N,
-                                  int S, int cap, int num_slots, int max_segments,
-                                  int row_tile) {
+// Persistent grid over items = (segment sub-tile of row_tile tokens, block of
+// blockDim.x * kColsPerThread output columns).  Per item: the sub-tile's rows and
+// their z values (FP32, zero past the rank) are staged in shared memory, then each
+// thread updates its columns for every row of the sub-tile.
+template <bool PAIRED>
+__global__ void __launch_bounds__(256, 4) row_expand_kernel(
+    const uint16_t* __restrict__ z, const uint16_t* __restrict__ B,
+    const int64_t* __restrict__ b_offsets, const int32_t* __restrict__ b_strides, uint16_t* y,
+    int64_t y_stride, const int32_t* __restrict__ indptr, const int32_t* __restrict__ seg_slots,
+    const int32_t* __restrict__ perm, const int32_t* __restrict__ ranks,
+    const float* __restrict__ scales, const int32_t* __restrict__ slice_offsets,
+    const int32_t* __restrict__ seg_count, int T_tokens, int N, int S, int cap, int num_slots,
+    int max_segments, int row_tile) {
   __shared__ int rows[kSegRows];
   __shared__ int offs[kMaxSlices + 1];
-  __shared__ float zs[kSegRows * kMaxSlices * 64];
+  __shared__ __align__(16) float zs[kSegRows * kMaxSlices * 64];
+  __shared__ uint32_t ys_all[kSegRows * 256];  // old y: both columns of a token, per thread
   const int tid = threadIdx.x;
   if (tid <= S) offs[tid] = slice_offsets[tid];
   const int parts = kSegRows / row_tile;
-  const int column_blocks = (N + blockDim.x - 1) / blockDim.x;
+  const int span = blockDim.x * kColsPerThread;
+  const int column_blocks = (N + span - 1) / span;
   const int nseg = min(*seg_count, max_segments);
   const int items = nseg * parts * column_blocks;
   for (int item = blockIdx.x; item < items; item += gridDim.x) {
@@ -92,40 +226,26 @@ __global__ void row_expand_kernel(const uint16_t* __restrict__ z, const uint16_t
     const int bucket = b_strides[g];
     if (rank <= 0 || rank > 64 || rank > cap) continue;
     if (bucket < 1 || bucket > 64 || (bucket & (bucket - 1))) continue;
-    __syncthreads();  // the previous item is done with rows/zs
+    __syncthreads();  // the previous item is done with rows and zs
+    int row = -1;
     if (tid < T) {
-      const int row = perm[start + tid];
-      rows[tid] = (row >= 0 && row < T_tokens) ? row : -1;
+      row = perm[start + tid];
+      if (row < 0 || row >= T_tokens) row = -1;
+      rows[tid] = row;
     }
-    __syncthreads();
-    bool valid = true;
-    for (int t = 0; t < T; ++t) valid &= rows[t] >= 0;
-    if (!valid) continue;  // uniform: every thread read the same rows
-    for (int i = tid; i < T * S * bucket; i += blockDim.x) {
-      const int t = i / (S * bucket);
-      const int rem = i - t * S * bucket;
-      const int s = rem / bucket;
-      const int k = rem - s * bucket;
-      zs[(t * kMaxSlices + s) * 64 + k] =
-          k < rank ? bf16_bits_to_float(z[int64_t(rows[t]) * S * cap + s * rank + k]) : 0.f;
-    }
-    __syncthreads();
-    const int n = cb * blockDim.x + tid;
-    if (n < N) {
-      int slice = 0;
-      for (int i = 1; i < S; ++i)
-        if (n >= offs[i]) slice = i;
-      const uint16_t* bp = B + b_offsets[g];
-      const float scale = scales[g];
-      switch (bucket) {
-        case 1: expand_column<1>(bp, y, y_stride, n, slice, T, rows, zs, scale); break;
-        case 2: expand_column<2>(bp, y, y_stride, n, slice, T, rows, zs, scale); break;
-        case 4: expand_column<4>(bp, y, y_stride, n, slice, T, rows, zs, scale); break;
-        case 8: expand_column<8>(bp, y, y_stride, n, slice, T, rows, zs, scale); break;
-        case 16: expand_column<16>(bp, y, y_stride, n, slice, T, rows, zs, scale); break;
-        case 32: expand_column<32>(bp, y, y_stride, n, slice, T, rows, zs, scale); break;
-        default: expand_column<64>(bp, y, y_stride, n, slice, T, rows, zs, scale); break;
-      }
+    if (__syncthreads_or(tid < T && row < 0)) continue;  // uniform: one bad row skips the item
+    const int base = cb * span;
+    const uint16_t* bslot = B + b_offsets[g];
+    const float scale = scales[g];
+    uint32_t* ys = ys_all + tid;
+    switch (bucket) {  // uniform across the CTA: expand_item's barrier is reached by all
+      case 1: expand_item<1, PAIRED>(z, bslot, y, y_stride, base, N, offs, S, cap, rank, T, rows, zs, scale, ys); break;
+      case 2: expand_item<2, PAIRED>(z, bslot, y, y_stride, base, N, offs, S, cap, rank, T, rows, zs, scale, ys); break;
+      case 4: expand_item<4, PAIRED>(z, bslot, y, y_stride, base, N, offs, S, cap, rank, T, rows, zs, scale, ys); break;
+      case 8: expand_item<8, PAIRED>(z, bslot, y, y_stride, base, N, offs, S, cap, rank, T, rows, zs, scale, ys); break;
+      case 16: expand_item<16, PAIRED>(z, bslot, y, y_stride, base, N, offs, S, cap, rank, T, rows, zs, scale, ys); break;
+      case 32: expand_item<32, PAIRED>(z, bslot, y, y_stride, base, N, offs, S, cap, rank, T, rows, zs, scale, ys); break;
+      default: expand_item<64, PAIRED>(z, bslot, y, y_stride, base, N, offs, S, cap, rank, T, rows, zs, scale, ys); break;
     }
   }
 }
@@ -272,17 +392,28 @@ extern "C" int lf_row_expand(const void* z, const void* b, const int64_t* b_offs
   if (num_slices < 1 || num_slices > kMaxSlices || capacity < 1 || num_slots < 1)
     return fail(LF_E_INVALID, "row_expand: invalid slice count, capacity or slot count");
   if (threads != 128 && threads != 256) return fail(LF_E_INVALID, "row_expand: threads must be 128 or 256");
-  if (blocks < 1 || blocks > 65535) return fail(LF_E_INVALID, "row_expand: blocks must be in 1..65535");
+  if (blocks < 0 || blocks > 65535) return fail(LF_E_INVALID, "row_expand: blocks must be in 0..65535");
   if (row_tile != 2 && row_tile != 4 && row_tile != 8 && row_tile != 16)
     return fail(LF_E_INVALID, "row_tile must be 2, 4, 8, or 16");
   if (y_stride < out_width || !aligned16(b))
     return fail(LF_E_INVALID, "row_expand: expected aligned B and nonoverlapping output rows");
   if (max_segments < 0) return fail(LF_E_INVALID, "row_expand: negative segment capacity");
   if (num_tokens == 0 || max_segments == 0) return LF_OK;
-  const int column_blocks = (out_width + threads - 1) / threads;
+  const int span = threads * kColsPerThread;
+  const int column_blocks = (out_width + span - 1) / span;
   if (int64_t(max_segments) * (kSegRows / row_tile) * column_blocks >= (int64_t(1) << 31))
     return fail(LF_E_INVALID, "row_expand: segment work count must fit signed int32 indexing");
-  row_expand_kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
+  // Adjacent column pairs move as one 4-byte value when every row start is 4-byte aligned.
+  const bool paired = y_stride % 2 == 0 && (reinterpret_cast<uintptr_t>(y) & 3u) == 0;
+  auto kernel = paired ? row_expand_kernel<true> : row_expand_kernel<false>;
+  if (blocks == 0) {  // automatic: every CTA the SMs hold at once
+    int device = 0, sms = 0, per_sm = 0;
+    cudaGetDevice(&device);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, 0);
+    blocks = max(1, min(65535, sms * max(1, per_sm)));
+  }
+  kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint16_t*>(z), static_cast<const uint16_t*>(b), b_offsets, b_strides,
       static_cast<uint16_t*>(y), y_stride, segment_indptr, segment_slots, token_indices, ranks,
       scales, slice_offsets, segment_count, int(num_tokens), out_width, num_slices, capacity,

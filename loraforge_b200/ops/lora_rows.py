@@ -160,8 +160,8 @@ def row_expand(
     if not z.shape[0]:
         return
     with torch.cuda.device(z.device):
-        if blocks is None:  # two resident blocks per SM
-            blocks = 2 * torch.cuda.get_device_properties(z.device).multi_processor_count
+        if blocks is None:  # 0: the kernel's own resident-CTA count times the SMs
+            blocks = 0
         _launch_row_expand(
             z, b, b_offsets, b_strides, output, segment_indptr, segment_slots,
             token_indices, ranks, scales, slice_offsets, segment_count,
