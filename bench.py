@@ -59,6 +59,7 @@ L2_NOTE = "flushed before every timed step (256 MiB write, outside the step even
 TRAFFIC = {
     (1, "fused", "gate_up_proj.fused"): (19.430144 + 75.358720 + 3.842816) * 1e6,
     (2, "fused", "proj.fused"): (51.121664 + 0.143360 + 49.703424 + 0.023040) * 1e6,
+    (4, "fused", "gate_up_proj.fused"): (145.522688 + 3.292672 + 822.391040 + 51.766784) * 1e6,
 }
 
 
