@@ -1,25 +1,22 @@
-// Slot-major LoRA shrink (z = A_g · x_t for every token t routed to slot g).
+// LoRA shrink kernels: z = A_g · x_t for every token t routed to slot g.
 //
-// The reference launches one CTA per token and one warp per (token, rank row), so
-// every token re-reads its adapter's A rows (src/loraforge/ops/csrc/lora_rows.cu:35-65,
-// grid at :178-180).  Here a CTA finds the tokens routed to its slot with a ballot scan
-// of the routing vector and streams the slot's A rows once for all of them; K is split
-// across a thread-block cluster of up to 8 CTAs whose partial sums are added in a fixed
-// order through distributed shared memory, so results are deterministic and no
-// scratch memory or atomics are needed.
-//
-// Two kernels:
-//   slot_shrink_mma_kernel  BF16 / FP16 with 16-byte aligned rows: grid (slot, K part),
-//                           tensor cores (mma.sync), every token of the slot in one
-//                           pass of up to 32 tokens.
-//   slot_shrink_kernel      every other case (FP32, unaligned rows): grid (slot, block
-//                           of 16 A rows, K part), CUDA-core FMAs over tiles of 8
-//                           tokens staged in shared memory as FP32.
+//   token_shrink_kernel  BF16 / FP16 operands with 16-byte aligned rows (the row_shrink,
+//                        fleet direct_shrink, padded BGMV and vLLM shrinks on their usual
+//                        inputs): one CTA per (token, 8 A rows), one warp per row, each row
+//                        summed in the reference's order, so BF16 z is bit-identical to the
+//                        reference kernel's (src/loraforge/ops/csrc/lora_rows.cu:35-65).
+//   slot_shrink_kernel   every other case (FP32 operands, unaligned rows): grid (slot, block
+//                        of 16 A rows, K part); a CTA finds its slot's tokens with a ballot
+//                        scan of the routing vector, stages tiles of up to 8 of their x rows
+//                        in shared memory as FP32 and streams its A rows once per tile; K is
+//                        split across a thread-block cluster of up to 8 CTAs whose partial
+//                        sums are added in a fixed order through distributed shared memory.
 //
 // Both serve three operand layouts through a small policy struct:
 //   RetainedShrink  — retained-rank BF16 (row_shrink / fleet direct_shrink);
 //   PaddedShrink    — SGLang padded-A decode layout (lora_shrink), any float dtype;
 //   VllmShrink      — vLLM per-slice padded layout with FP32 output (vllm_gemv.shrink).
+// Results are deterministic (no atomics) and no scratch memory is used.
 #include <cooperative_groups.h>
 
 #include <type_traits>
@@ -328,255 +325,85 @@ inline int k_parts(int64_t K) {
   return int(p < 1 ? 1 : (p > 8 ? 8 : p));
 }
 
-// ------------------------------------------------------------------ tensor-core kernel
-// BF16 / FP16 operands with 16-byte aligned rows.  Grid (slot, K part), the K parts of a
-// slot forming a cluster: one CTA covers every A row of its slot, so the routing vector
-// is scanned once per (slot, K part), and every token of the slot is handled in one
-// pass over A (up to 32 tokens per pass) instead of one pass per 8 tokens, so a
-// popular slot no longer costs one A stream per token tile.
+// ------------------------------------------------------------------ token-major kernel
+// 16-bit operands with 16-byte aligned rows.  One CTA of eight warps per (token, group of
+// eight A rows), one warp per row, like the reference (src/loraforge/ops/csrc/lora_rows.cu:
+// 35-65, grid at :178-180), and every row summed in the reference's order: lane l takes
+// the 8-element chunks starting at 8l, 8l + 256, ... and accumulates their products with
+// fused multiply-adds in element order, then the lanes' sums are added by the same
+// shuffle-down tree (offsets 16, 8, 4, 2, 1).  The FP32 dot products, and the BF16 z after
+// rounding, are therefore bit-identical to the reference kernel's on the same inputs.
 //
-// The slot's tokens are the M dimension of mma.sync m16n8k16 (two m16 tiles) and its
-// A rows the N dimension, in blocks of 16 rows (two n8 tiles); operands go from global
-// memory straight into fragment registers.  Inside each 32-column k block both
-// operands carry the same permutation of k (lane t holds columns 8t..8t+7 of its
-// row), so one 16-byte load per lane and row feeds two MMAs.  Warp w takes the k
-// blocks w, w+8, ... of the CTA's K part, two at a time: the x fragments of a pair are
-// loaded once and used for both row blocks of a 32-row group (holding more row blocks
-// at once spilled registers and measured slower).  The eight warps' products are summed in
-// warp order in shared memory, and the K parts in part order through distributed
-// shared memory, so results are deterministic and no scratch memory is needed.
-constexpr int kMmaWarps = 8;
-constexpr int kMmaThreads = kMmaWarps * 32;
-constexpr int kMmaTok = 32;       // tokens per pass (two m16 tiles)
-constexpr int kMmaBlocks = 2;     // row blocks of 16 held at once (32 rows)
-constexpr int kMmaRows = kMmaBlocks * 16;
-constexpr int kMmaWindow = 2048;
+// Each chunk's A load (the long-latency stream: HBM, or L2 for a popular slot's later
+// tokens) is issued before its x load (L1 after the first warp of the CTA); that order
+// measured 25-35 % faster than x first at the same arithmetic, and the unrolled loop keeps
+// several chunks in flight.  A slot-major kernel on the tensor cores (one CTA per slot and
+// K part, every token of the slot in one pass, K parts summed through distributed shared
+// memory) read each A row once but measured slower on config 1 (qkv 36.8, gate_up 26.5,
+// down 32.9 us against 20.4, 18.4, 26.5): its chain of scan, copy and reduction latencies
+// left the SMs idle.
+constexpr int kTokWarps = 8;
+constexpr int kTokThreads = kTokWarps * 32;
 
 template <typename T>
-__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
-                                          uint32_t a3, uint32_t b0, uint32_t b1) {
-  if constexpr (std::is_same<T, f16_t>::value) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-        "{%8,%9}, {%0,%1,%2,%3};\n"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-  } else {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-        "{%8,%9}, {%0,%1,%2,%3};\n"
-        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+__device__ __forceinline__ void unpack8(const uint4& v, float* out);
+template <>
+__device__ __forceinline__ void unpack8<bf16_t>(const uint4& v, float* out) {
+  unpack_bf16x8(v, out);
+}
+template <>
+__device__ __forceinline__ void unpack8<f16_t>(const uint4& v, float* out) {
+  const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(h[i]);
+    out[2 * i] = f.x;
+    out[2 * i + 1] = f.y;
   }
 }
 
-struct MmaShrinkSmem {
-  int list[kMmaWindow];
-  float red[kMmaWarps][kMmaTok][kMmaRows];  // per-warp products of a pass
-  float part[kMmaTok][kMmaRows];            // this CTA's sum, read by the cluster's rank 0
-  int warp_count[kMmaWarps];
-  int list_len;
-};
-
 template <typename T, typename L>
-__global__ void __launch_bounds__(kMmaThreads, 2)
-slot_shrink_mma_kernel(const __grid_constant__ L layout, const typename T::storage* __restrict__ x,
-                       int64_t x_stride, int T_tokens, int64_t K) {
+__global__ void __launch_bounds__(kTokThreads)
+token_shrink_kernel(const __grid_constant__ L layout, const typename T::storage* __restrict__ x,
+                    int64_t x_stride, int K) {
   using S = typename T::storage;
-  extern __shared__ __align__(16) uint8_t smem_raw[];
-  MmaShrinkSmem& sm = *reinterpret_cast<MmaShrinkSmem*>(smem_raw);
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int g = lane >> 2, t = lane & 3;
-  const int slot = blockIdx.x;
+  const int t = blockIdx.x;
+  const int g = layout.slot_of(t);
+  if (g < 0) return;
   typename L::State st;
-  const int nrows = layout.prepare(slot, st);
-  if (nrows <= 0) return;  // uniform across the cluster (same slot)
-
-  const int parts = gridDim.y;
-  const int64_t nkb_all = (K + 31) / 32;
-  const int64_t per_part = (nkb_all + parts - 1) / parts;  // k blocks per part
-  const int64_t kb0 = min(nkb_all, int64_t(blockIdx.y) * per_part);
-  const int64_t kb1 = min(nkb_all, kb0 + per_part);
-
-  const unsigned lower = (1u << lane) - 1u;
-  for (int w0 = 0; w0 < T_tokens; w0 += kMmaWindow) {
-    const int wend = min(T_tokens, w0 + kMmaWindow);
-    // Ballot scan of the routing window: the list keeps token order.
-    if (tid == 0) sm.list_len = 0;
-    __syncthreads();
-    for (int base = w0; base < wend; base += kMmaThreads) {
-      const int tk = base + tid;
-      const bool mine = tk < wend && layout.slot_of(tk) == slot;
-      const unsigned ballot = __ballot_sync(0xffffffffu, mine);
-      if (lane == 0) sm.warp_count[warp] = __popc(ballot);
-      __syncthreads();
-      int offset = sm.list_len;
-      for (int w = 0; w < warp; ++w) offset += sm.warp_count[w];
-      if (mine) sm.list[offset + __popc(ballot & lower)] = tk;
-      __syncthreads();
-      if (tid == 0) {
-        int total = 0;
-        for (int w = 0; w < kMmaWarps; ++w) total += sm.warp_count[w];
-        sm.list_len += total;
-      }
-      __syncthreads();
-    }
-    const int n = sm.list_len;
-    for (int tb = 0; tb < n; tb += kMmaTok) {
-      const int ntok = min(kMmaTok, n - tb);
-      const int mtiles = (ntok + 15) >> 4;
-      // x rows of this lane in each m tile (rows g and g + 8); null past the pass.
-      const S* xrow[2][2];
+  const int nrows = layout.prepare(g, st);
+  const int lane = threadIdx.x & 31;
+  const int j = blockIdx.y * kTokWarps + (threadIdx.x >> 5);
+  if (j >= nrows) return;  // no barrier in this kernel: warps leave independently
+  const S* arow = layout.a_row(g, j, st);
+  if (arow == nullptr) return;
+  const S* xr = x + int64_t(t) * x_stride;
+  float acc = 0.f;
+#pragma unroll 8
+  for (int k = lane * 8; k < K; k += 256) {
+    const uint4 av = *reinterpret_cast<const uint4*>(arow + k);  // A first: the long-latency stream
+    const uint4 xv = *reinterpret_cast<const uint4*>(xr + k);
+    float a8[8], x8[8];
+    unpack8<T>(av, a8);
+    unpack8<T>(xv, x8);
 #pragma unroll
-      for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int m = mt * 16 + g + 8 * h;
-          xrow[mt][h] = m < ntok ? x + int64_t(sm.list[tb + m]) * x_stride : nullptr;
-        }
-      for (int r0 = 0; r0 < nrows; r0 += kMmaRows) {  // groups of kMmaBlocks row blocks
-        const int blocks = min(kMmaBlocks, (nrows - r0 + 15) >> 4);
-        // This lane's A rows: row block b, n tile nt, row g (null past the slot's rows).
-        const S* arow[kMmaBlocks][2];
-#pragma unroll
-        for (int b = 0; b < kMmaBlocks; ++b)
-#pragma unroll
-          for (int nt = 0; nt < 2; ++nt) {
-            const int j = r0 + b * 16 + nt * 8 + g;
-            arow[b][nt] = (b < blocks && j < nrows) ? layout.a_row(slot, j, st) : nullptr;
-          }
-        float d[kMmaBlocks][2][2][4];  // [row block][m tile][n tile][4]
-#pragma unroll
-        for (int b = 0; b < kMmaBlocks; ++b)
-#pragma unroll
-          for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt) d[b][mt][nt][0] = d[b][mt][nt][1] = d[b][mt][nt][2] = d[b][mt][nt][3] = 0.f;
-
-        for (int64_t kb = kb0 + warp; kb < kb1; kb += 2 * kMmaWarps) {
-          // x fragments of the two k blocks kb and kb + 8 (zero past K or the pass).
-          uint4 xf[2][2][2];  // [k block][m tile][row half]
-#pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            const int64_t k = (kb + q * kMmaWarps) * 32 + 8 * t;
-            const bool live = kb + q * kMmaWarps < kb1 && k < K;  // K is a multiple of 8
-#pragma unroll
-            for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-              for (int h = 0; h < 2; ++h)
-                xf[q][mt][h] = (live && mt < mtiles && xrow[mt][h])
-                                   ? *reinterpret_cast<const uint4*>(xrow[mt][h] + k)
-                                   : make_uint4(0, 0, 0, 0);
-          }
-#pragma unroll
-          for (int b = 0; b < kMmaBlocks; ++b) {
-            if (b >= blocks) continue;
-            uint4 af[2][2];  // [k block][n tile]
-#pragma unroll
-            for (int q = 0; q < 2; ++q) {
-              const int64_t k = (kb + q * kMmaWarps) * 32 + 8 * t;
-              const bool live = kb + q * kMmaWarps < kb1 && k < K;
-#pragma unroll
-              for (int nt = 0; nt < 2; ++nt)
-                af[q][nt] = (live && arow[b][nt]) ? *reinterpret_cast<const uint4*>(arow[b][nt] + k)
-                                                  : make_uint4(0, 0, 0, 0);
-            }
-#pragma unroll
-            for (int q = 0; q < 2; ++q)
-#pragma unroll
-              for (int mt = 0; mt < 2; ++mt) {
-                if (mt >= mtiles) continue;
-#pragma unroll
-                for (int nt = 0; nt < 2; ++nt) {
-                  const uint4& xa = xf[q][mt][0];
-                  const uint4& xb = xf[q][mt][1];
-                  const uint4& w = af[q][nt];
-                  mma_16816<T>(d[b][mt][nt], xa.x, xb.x, xa.y, xb.y, w.x, w.y);
-                  mma_16816<T>(d[b][mt][nt], xa.z, xb.z, xa.w, xb.w, w.z, w.w);
-                }
-              }
-          }
-        }
-        // Per-warp products -> shared memory: accumulator (b, mt, nt) holds tokens
-        // mt*16 + g (+8) and rows b*16 + nt*8 + 2t (+1) of the group.
-#pragma unroll
-        for (int b = 0; b < kMmaBlocks; ++b)
-#pragma unroll
-          for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt) {
-              if (b >= blocks || mt >= mtiles) continue;
-              const int c = b * 16 + nt * 8 + 2 * t;
-              *reinterpret_cast<float2*>(&sm.red[warp][mt * 16 + g][c]) = make_float2(d[b][mt][nt][0], d[b][mt][nt][1]);
-              *reinterpret_cast<float2*>(&sm.red[warp][mt * 16 + g + 8][c]) = make_float2(d[b][mt][nt][2], d[b][mt][nt][3]);
-            }
-        __syncthreads();
-        const int width = blocks * 16;
-        for (int e = tid; e < ntok * width; e += kMmaThreads) {
-          const int m = e / width, r = e - m * width;
-          float s = 0.f;
-#pragma unroll
-          for (int w = 0; w < kMmaWarps; ++w) s += sm.red[w][m][r];
-          sm.part[m][r] = s;
-        }
-        if (parts == 1) {
-          __syncthreads();
-          for (int e = tid; e < ntok * width; e += kMmaThreads) {
-            const int m = e / width, r = e - m * width, j = r0 + r;
-            if (j < nrows && layout.a_row(slot, j, st) != nullptr) layout.store(sm.list[tb + m], j, sm.part[m][r], st);
-          }
-          __syncthreads();
-        } else {
-          cg::cluster_group cluster = cg::this_cluster();
-          cluster.sync();
-          if (cluster.block_rank() == 0) {
-            for (int e = tid; e < ntok * width; e += kMmaThreads) {
-              const int m = e / width, r = e - m * width, j = r0 + r;
-              if (j < nrows && layout.a_row(slot, j, st) != nullptr) {
-                float s = 0.f;
-                for (int q = 0; q < parts; ++q) s += cluster.map_shared_rank(&sm.part[0][0], q)[m * kMmaRows + r];
-                layout.store(sm.list[tb + m], j, s, st);
-              }
-            }
-          }
-          cluster.sync();
-        }
-      }
-    }
+    for (int e = 0; e < 8; ++e) acc = fmaf(a8[e], x8[e], acc);
   }
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) acc += __shfl_down_sync(0xffffffffu, acc, d);
+  if (lane == 0) layout.store(t, j, acc, st);
 }
 
 template <typename T, typename L>
-int launch_shrink_mma(const L& layout, const typename T::storage* x, int64_t x_stride,
-                      int64_t T_tokens, int64_t K, int num_slots, cudaStream_t stream,
-                      const char* what) {
-  static int flags[64] = {};
-  auto kernel = slot_shrink_mma_kernel<T, L>;
-  constexpr int smem = int(sizeof(MmaShrinkSmem));
-  if (int rc = ensure_smem(kernel, smem, flags)) return rc;
-  // About one CTA per 512 input columns, at most 8 (a portable cluster).
-  const int64_t want = (K + 511) / 512;
-  const int parts = int(want < 1 ? 1 : (want > 8 ? 8 : want));
-  const dim3 grid(num_slots, parts);
-  cudaError_t err;
-  if (parts == 1) {
-    kernel<<<grid, kMmaThreads, smem, stream>>>(layout, x, x_stride, int(T_tokens), K);
-    err = cudaGetLastError();
-  } else {
-    cudaLaunchConfig_t config = {};
-    config.gridDim = grid;
-    config.blockDim = dim3(kMmaThreads);
-    config.dynamicSmemBytes = smem;
-    config.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = parts;
-    attr[0].val.clusterDim.z = 1;
-    config.attrs = attr;
-    config.numAttrs = 1;
-    err = cudaLaunchKernelEx(&config, kernel, layout, x, x_stride, int(T_tokens), K);
-  }
+int launch_token_shrink(const L& layout, const typename T::storage* x, int64_t x_stride,
+                        int64_t T_tokens, int64_t K, int max_rows, cudaStream_t stream,
+                        const char* what) {
+  const int groups = (max_rows + kTokWarps - 1) / kTokWarps;
+  if (groups < 1 || groups > 65535) return fail(LF_E_INVALID, "shrink: too many rank rows");
+  if (K >= (int64_t(1) << 31) - 256) return fail(LF_E_INVALID, "shrink: width too large");
+  token_shrink_kernel<T, L><<<dim3(unsigned(T_tokens), unsigned(groups)), kTokThreads, 0, stream>>>(
+      layout, x, x_stride, int(K));
+  const cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) {
     last_error() = std::string(what) + ": " + cudaGetErrorString(err);
     return LF_E_CUDA;
@@ -619,7 +446,7 @@ int dispatch_vec(const L& layout, const void* x, int64_t x_stride, int64_t T_tok
   const S* xp = static_cast<const S*>(x);
   if constexpr (!std::is_same<T, f32_t>::value) {
     if (vec_ok)
-      return launch_shrink_mma<T>(layout, xp, x_stride, T_tokens, K, num_slots, stream, what);
+      return launch_token_shrink<T>(layout, xp, x_stride, T_tokens, K, max_rows, stream, what);
   }
   if (vec_ok)
     return launch_shrink<T, V>(layout, xp, x_stride, T_tokens, K, num_slots, max_rows, stream,
