@@ -68,7 +68,7 @@ constexpr int kRedPitch = 72;  // floats per row of the cross-warp reduction buf
 constexpr int kRedBytes = kConsumerWarps * kSeg * kRedPitch * 4;
 constexpr int kHeaderBytes = 128;
 constexpr int kMaxStages = 8;
-constexpr int kStageBudget = 104 * 1024;  // per CTA: two CTAs share an SM
+constexpr int kStageBudget = 110 * 1024;  // per CTA: two CTAs share an SM (228 KiB, 1 KiB reserved each)
 
 enum Numerics { kFp32 = 0, kReference = 1 };
 
@@ -1077,14 +1077,17 @@ inline int shrink_stage_bytes(int rstride, int kc) {
   return round_up(kSeg * (kc * 2 + kRowPad) + rstride * kc * 2 + kHeaderBytes, 128);
 }
 
-// Register path (S*r <= 64): two CTAs per SM.  Wide path: one.
+// Register path (S*r <= 64): two CTAs per SM.  Wide path: one.  The K chunk is the widest
+// of 512 / 256 / 128 columns whose stage fits 52 KiB: each unit reads a chunk-wide piece of
+// every live A row, and 1 KiB pieces (kc = 512) stream from HBM markedly faster than 512-byte
+// ones when a projection's rows are long (rank 32, K = 27648: 148.8 -> 128.8 us per call).
 inline ShrinkConfig shrink_config(int64_t width, int num_slices, int capacity) {
   ShrinkConfig c{};
   c.rstride = round_up(num_slices * (capacity < kMaxRank ? capacity : kMaxRank), 8);
   const bool regs = c.rstride <= 64;
   int kc = 64;
   for (int cand : {512, 256, 128}) {
-    if (shrink_stage_bytes(c.rstride, cand) <= 48 * 1024) {
+    if (shrink_stage_bytes(c.rstride, cand) <= 52 * 1024) {
       kc = cand;
       break;
     }
