@@ -96,6 +96,7 @@ struct Params {
   int kc, nchunks;
   int stages, stage_bytes;  // of the kernel being launched
   int max_tokens;           // longer segments are left to the prefill (tcgen05) kernels
+  int bstage;               // expand: bytes of B rows per stage (16 or 32 KiB)
   CUtensorMap tmap_a;  // A as 2-D [slots*S*cap rows, K], boxes of 8 rows x min(kc, 256)
   // The same with boxes of 64 / 32 / 16 rows: for kc <= 256 the 8-row groups of a stage are
   // plain row-major, so fewer, taller boxes fill the same layout.
@@ -559,7 +560,6 @@ __global__ void __launch_bounds__(kThreads, REGS ? 2 : 1)
 
 // ====================================================================== expand
 constexpr int kStageCols = 512;                  // output columns per expand stage (max)
-constexpr int kBStage = 16 * 1024;               // bytes of B rows per expand stage
 constexpr int kYStagePitch = kStageCols * 2 + kRowPad;
 
 struct alignas(16) ExpandHeader {
@@ -676,7 +676,7 @@ __device__ __forceinline__ void expand_stage(const Params& p, const ExpandHeader
       const int m = g + 8 * hh;
       if constexpr (STAGED) {
         uint4 w = make_uint4(0, 0, 0, 0);
-        if (mine && m < h.n) w = lds16(st + kBStage + m * kYStagePitch + my * 2);
+        if (mine && m < h.n) w = lds16(st + p.bstage + m * kYStagePitch + my * 2);
         unpack_bf16x8(w, v);
       } else {
 #pragma unroll
@@ -783,7 +783,7 @@ __device__ __forceinline__ void expand_stage_pair(const Params& p, const ExpandH
         const int m = g + 8 * hh;
         float v[8];
         uint4 w = make_uint4(0, 0, 0, 0);
-        if (MODE == kFp32 && mine[q] && m < h.n) w = lds16(st + kBStage + m * kYStagePitch + my[q] * 2);
+        if (MODE == kFp32 && mine[q] && m < h.n) w = lds16(st + p.bstage + m * kYStagePitch + my[q] * 2);
         unpack_bf16x8(w, v);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -822,7 +822,7 @@ __device__ __forceinline__ void expand_stage_pair(const Params& p, const ExpandH
         for (int c = 0; c < 8; ++c) v[c] = d[q][c >> 1][2 * hh + (c & 1)];
         if (MODE != kFp32) {
           float yv[8];
-          unpack_bf16x8(lds16(st + kBStage + m * kYStagePitch + my[q] * 2), yv);
+          unpack_bf16x8(lds16(st + p.bstage + m * kYStagePitch + my[q] * 2), yv);
 #pragma unroll
           for (int c = 0; c < 8; ++c) v[c] = yv[c] + round_through_bf16(v[c] * h.scale);
         }
@@ -966,7 +966,7 @@ __global__ void __launch_bounds__(kThreads, 2) sgmv_expand_kernel(const __grid_c
     // B rows and y rows do not depend on the shrink: no griddepcontrol.wait here.
     const int u0 = split_bounds[0], u1 = split_bounds[1];
     // Consecutive 128-column units of one segment are merged into a stage while its
-    // B rows fit kBStage and its columns kStageCols.
+    // B rows fit p.bstage and its columns kStageCols.
     int cur = -1, tok = -1;
     Seg si{};
     Ring ring;
@@ -982,7 +982,7 @@ __global__ void __launch_bounds__(kThreads, 2) sgmv_expand_kernel(const __grid_c
         u = min(u1, (seg + 1) * ncb);
         continue;
       }
-      const int max_cols = min(kStageCols, kBStage / (2 * si.bucket));  // >= kExpandCols
+      const int max_cols = min(kStageCols, p.bstage / (2 * si.bucket));  // >= kExpandCols
       const int take = min(min(max_cols / kExpandCols, ncb - cb), u1 - u);
       const int c0 = cb * kExpandCols;
       const int nc = min(p.N, (cb + take) * kExpandCols) - c0;
@@ -1025,7 +1025,7 @@ __global__ void __launch_bounds__(kThreads, 2) sgmv_expand_kernel(const __grid_c
       __syncwarp();
       if (lane == 31 && bbulk) bulk_g2s(st, bsrc, bbulk, &full[stage]);
       if (STAGED && lane < si.n)
-        bulk_g2s(st + kBStage + lane * kYStagePitch, p.y + int64_t(tok) * p.y_stride + c0, ybytes,
+        bulk_g2s(st + p.bstage + lane * kYStagePitch, p.y + int64_t(tok) * p.y_stride + c0, ybytes,
                  &full[stage]);
     }
     if (alive) {  // end of stream
@@ -1125,9 +1125,18 @@ struct ExpandConfig {
   int stages, stage_bytes, smem;
 };
 
-inline ExpandConfig expand_config(bool staged) {
+// B rows per stage: 32 KiB when a slot's bucket can reach 32 (a 512-column stage of rank-32
+// rows: half as many stages, each moving twice the bytes; config 4 390 -> 371 us/step,
+// config 2 71.0 -> 68.0), else 16 KiB, which keeps three stages in flight for rank-16 and
+// smaller buckets (their 512 columns fit 16 KiB; 32 KiB stages measured 102.7 -> 108.7 us/step
+// on config 1).
+inline int expand_bstage(int capacity) {
+  return (capacity > 16 ? 32 : 16) * 1024;
+}
+
+inline ExpandConfig expand_config(bool staged, int bstage) {
   ExpandConfig c{};
-  c.stage_bytes = round_up(kBStage + (staged ? kSeg * kYStagePitch : 0) + kHeaderBytes, 128);
+  c.stage_bytes = round_up(bstage + (staged ? kSeg * kYStagePitch : 0) + kHeaderBytes, 128);
   int stages = kStageBudget / c.stage_bytes;
   c.stages = stages < 2 ? 2 : (stages > kMaxStages ? kMaxStages : stages);
   c.smem = c.stages * c.stage_bytes + 2 * kMaxStages * 8 + (kMaxSlices + 4) * 4;
@@ -1294,7 +1303,8 @@ int fused_launch(const void* x, int64_t x_stride, const void* a, const void* b,
   if (num_tokens == 0 || max_segments == 0) return LF_OK;
   const bool staged = out_width % 8 == 0 && y_stride % 8 == 0 &&
                       (reinterpret_cast<uintptr_t>(y) & 15) == 0;
-  const ExpandConfig ec = expand_config(staged);
+  const int bstage = expand_bstage(capacity);
+  const ExpandConfig ec = expand_config(staged, bstage);
   const int64_t T = num_tokens;
   Params p{static_cast<const uint16_t*>(x), x_stride, static_cast<const uint16_t*>(a),
            static_cast<const uint16_t*>(b), b_offsets, b_strides, static_cast<uint16_t*>(y),
@@ -1344,6 +1354,7 @@ int fused_launch(const void* x, int64_t x_stride, const void* a, const void* b,
   if (!(phases & kPhaseExpand)) return LF_OK;
   p.stages = ec.stages;
   p.stage_bytes = ec.stage_bytes;
+  p.bstage = bstage;
   const int64_t units = seg_cap * ((out_width + kExpandCols - 1) / kExpandCols);
   const int grid = int(units < 2 * sms ? units : 2 * sms);
   auto kernel = numerics == kFp32
