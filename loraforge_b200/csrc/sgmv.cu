@@ -43,15 +43,19 @@
 //
 // Every mbarrier wait is bounded (tma.cuh); consumers agree on an expired wait with a
 // barrier vote before leaving their loop, so no thread is left at a named barrier.
+#include <cooperative_groups.h>
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
 #include <string>
 
 #include "launch.cuh"
 #include "sgmv.cuh"
 #include "tma.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace lfb {
 namespace {
@@ -582,13 +586,18 @@ __device__ __forceinline__ int slice_of(const int* offs, int S, int col) {
 // z fragments of slice s for this lane, multiplied by `mul`: [mma q][hi, lo][4 regs].
 // Every z value of the lane is loaded before the first is converted, so the loads
 // overlap instead of paying one L2 round trip each.
-template <int KP, int MODE>
+// ZS: z is the CTA's own shared-memory copy `zsm` (rows of kZsPitch floats, the segment's
+// token m at row m) instead of the workspace's z rows, read with plain loads.
+constexpr int kZsPitch = 64;
+
+template <int KP, int MODE, bool ZS = false>
 __device__ __forceinline__ void load_z(const Params& p, const ExpandHeader& h, int s, float mul,
-                                       int g, int t, uint32_t (&zf)[4][2][4]) {
+                                       int g, int t, uint32_t (&zf)[4][2][4],
+                                       const float* zsm = nullptr) {
   const int live = min(h.r, h.bucket);
   constexpr int NV = KP == 8 ? 4 : KP / 16 * 8;
-  const float* zr0 = p.zfinal + int64_t(h.pos0 + g) * p.rstride + s * h.r;
-  const float* zr1 = zr0 + int64_t(8) * p.rstride;
+  const float* zr0 = ZS ? zsm + g * kZsPitch + s * h.r : p.zfinal + int64_t(h.pos0 + g) * p.rstride + s * h.r;
+  const float* zr1 = zr0 + (ZS ? int64_t(8) * kZsPitch : int64_t(8) * p.rstride);
   float v[NV];
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
@@ -604,7 +613,8 @@ __device__ __forceinline__ void load_z(const Params& p, const ExpandHeader& h, i
       m = (j >> 1) & 1;
       kk = base + ((j >> 2) << 1) + (j & 1);
     }
-    v[i] = (g + 8 * m < h.n && kk < live) ? __ldcg((m ? zr1 : zr0) + kk) : 0.f;
+    const float* zp = (m ? zr1 : zr0) + kk;
+    v[i] = (g + 8 * m < h.n && kk < live) ? (ZS ? *zp : __ldcg(zp)) : 0.f;
   }
 #pragma unroll
   for (int i = 0; i < NV; i += 2) {
@@ -652,11 +662,11 @@ __device__ __forceinline__ void load_b(const uint8_t* bt, int cb, int bucket, in
 // One consumer warp, every 32-column group grp = warp, warp + 8, ... of a stage.
 // Tile j of a group holds the columns 8*(nu>>1) + 2j + (nu&1) for its n index nu, so
 // lane (g, t) ends up owning the 8 consecutive columns 8t..8t+7 of rows g and g+8.
-template <int KP, int MODE, bool STAGED>
+template <int KP, int MODE, bool STAGED, bool ZS = false>
 __device__ __forceinline__ void expand_stage(const Params& p, const ExpandHeader& h,
                                              const uint8_t* st, const int* offs,
                                              uint32_t (&zf)[4][2][4], int& zseg, int& zslice,
-                                             int lane, int warp) {
+                                             int lane, int warp, const float* zsm = nullptr) {
   constexpr int Q = KP >= 16 ? KP / 16 : 1;
   constexpr int PARTS = MODE == kFp32 ? 2 : 1;
   const int g = lane >> 2, t = lane & 3;
@@ -688,7 +698,7 @@ __device__ __forceinline__ void expand_stage(const Params& p, const ExpandHeader
     };
     for (int s = s_first; s <= s_last; ++s) {
       if (h.seg != zseg || s != zslice) {
-        load_z<KP, MODE>(p, h, s, mul, g, t, zf);
+        load_z<KP, MODE, ZS>(p, h, s, mul, g, t, zf, zsm);
         zseg = h.seg;
         zslice = s;
       }
@@ -757,15 +767,16 @@ __device__ __forceinline__ void expand_stage(const Params& p, const ExpandHeader
 // Stages whose columns lie in one slice, with y staged and bucket <= 16: each warp runs
 // two of its 32-column groups side by side (same arithmetic as expand_stage), so the y
 // loads, MMA chains and stores of one group overlap the latencies of the other.
-template <int KP, int MODE>
+template <int KP, int MODE, bool ZS = false>
 __device__ __forceinline__ void expand_stage_pair(const Params& p, const ExpandHeader& h,
                                                   const uint8_t* st, uint32_t (&zf)[4][2][4],
-                                                  int& zseg, int& zslice, int lane, int warp) {
+                                                  int& zseg, int& zslice, int lane, int warp,
+                                                  const float* zsm = nullptr) {
   constexpr int PARTS = MODE == kFp32 ? 2 : 1;
   const int g = lane >> 2, t = lane & 3;
   const float mul = MODE == kFp32 ? h.scale : 1.f;  // fp32: scale folded into z
   if (h.seg != zseg || h.slice != zslice) {
-    load_z<KP, MODE>(p, h, h.slice, mul, g, t, zf);
+    load_z<KP, MODE, ZS>(p, h, h.slice, mul, g, t, zf, zsm);
     zseg = h.seg;
     zslice = h.slice;
   }
@@ -1066,6 +1077,263 @@ __global__ void __launch_bounds__(kThreads, 2) sgmv_expand_kernel(const __grid_c
   }
 }
 
+// ====================================================================== one-launch decode
+// sgmv_cluster_kernel: a whole decode shrink -> expand in one launch, z kept in shared
+// memory (S*r <= 64).  One thread-block cluster of C CTAs per segment, CTA rank q of
+// segment s at blockIdx.x = s*C + q:
+//   1. the producer streams chunks [q*cpp, (q+1)*cpp) of K through the stage ring (the
+//      segment's x rows and its S*r live A rows, laid out as the shrink kernel's stages)
+//      and the consumers accumulate the CTA's part of z in registers (the shrink's
+//      register path);
+//   2. the CTA's partial goes to its shared memory; after a cluster barrier every CTA
+//      adds the C partials in rank order from the cluster's distributed shared memory, so
+//      all C CTAs hold the same z (deterministic, no workspace, no counters);
+//   3. rank q expands the output columns [q*upp, (q+1)*upp) x 128 of the segment with the
+//      expand kernel's stages and consumers, reading z from shared memory.
+// The producer issues its expand stages (B rows, y rows) as soon as its shrink stages are
+// issued, so they are in flight while the cluster sums z.  Every thread of the cluster
+// passes two cluster barriers exactly once, also after an expired wait: #1 between the
+// partials and their sum (the producer arrives as soon as its shrink stages are issued),
+// #2 at the end, so that no CTA leaves while a peer may still read its partial.
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait;" ::: "memory"); }
+
+template <int MODE, bool STAGED>
+__global__ void __launch_bounds__(kThreads, 2) sgmv_cluster_kernel(const __grid_constant__ Params p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ Seg seg_s;
+  __shared__ int tok_s[kSeg];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int NS = p.stages, SB = p.stage_bytes;
+  const int hoff = SB - kHeaderBytes;
+  const int xpitch = p.kc * 2 + kRowPad;
+  float* red = reinterpret_cast<float*>(smem + NS * SB);  // [warp][16 rows][8 cols]
+  float* zpart = red + kConsumerWarps * kSeg * 8;         // [16][kZsPitch]: this CTA's K part
+  float* zs = zpart + kSeg * kZsPitch;                    // [16][kZsPitch]: the segment's z
+  uint64_t* full = reinterpret_cast<uint64_t*>(zs + kSeg * kZsPitch);
+  uint64_t* empty = full + kMaxStages;
+  int* offs = reinterpret_cast<int*>(empty + kMaxStages);
+
+  if (tid == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    fence_mbar_init();
+  }
+  if (tid <= p.S) offs[tid] = p.slice_offsets[tid];
+  if (tid == kConsumers) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&p.tmap_a) : "memory");
+    for (int h = 0; h < 3; ++h) asm volatile("prefetch.tensormap [%0];" ::"l"(&p.tmap_a_rows[h]) : "memory");
+  }
+  __syncthreads();
+  pdl_wait();  // x, y and the metadata may come from the preceding grid
+  pdl_launch_dependents();
+
+  cg::cluster_group cluster = cg::this_cluster();
+  const int C = int(cluster.num_blocks());
+  const int q = int(cluster.block_rank());
+  const int seg = int(blockIdx.x) / C;
+  if (seg >= segment_total(p)) return;  // the whole cluster: one segment, one count
+  if (warp == kConsumerWarps) {
+    int tok;
+    const Seg s = load_segment_warp(p, seg, lane, tok);
+    if (lane < kSeg) tok_s[lane] = tok;
+    if (lane == 0) seg_s = s;
+  }
+  __syncthreads();
+  const Seg si = seg_s;
+  if (!si.ok) return;  // every CTA of the cluster read the same metadata
+  const int R = p.S * si.r;
+  const int cpp = (p.nchunks + C - 1) / C;
+  const int c0 = min(p.nchunks, q * cpp), c1 = min(p.nchunks, c0 + cpp);
+  const int ncb = (p.N + kExpandCols - 1) / kExpandCols;
+  const int upp = (ncb + C - 1) / C;
+  const int u0 = min(ncb, q * upp), u1 = min(ncb, u0 + upp);
+
+  if (warp == kConsumerWarps) {
+    // ------------------------------------------------------------ producer warp
+    Ring ring;
+    bool alive = true;
+    const int bw = p.kc < 256 ? p.kc : 256;
+    const int groups = (R + 7) >> 3;
+    const int row0 = si.g * p.S * p.cap;
+    const int tok = lane < kSeg ? tok_s[lane] : -1;
+    for (int c = c0; c < c1; ++c) {
+      const int stage = ring.stage;
+      const uint32_t phase = ring.phase;
+      ring.next(NS);
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait(&empty[stage], phase ^ 1u) ? 1 : 0;
+      if (!__shfl_sync(0xffffffffu, ok, 0)) {
+        alive = false;
+        break;
+      }
+      uint8_t* st = smem + stage * SB;
+      const int k0 = c * p.kc;
+      const int len = min(p.kc, p.K - k0);
+      const int boxes = (len + bw - 1) / bw;
+      const uint32_t row_bytes = uint32_t(len) * 2;
+      const uint32_t tx = uint32_t(si.n) * row_bytes + uint32_t(groups * boxes) * (8 * bw * 2);
+      __syncwarp();
+      if (lane == 0) mbar_arrive_expect_tx(&full[stage], tx);
+      __syncwarp();
+      if (lane < si.n)
+        bulk_g2s(st + lane * xpitch, p.x + int64_t(tok) * p.x_stride + k0, row_bytes, &full[stage]);
+      uint8_t* abase = st + kSeg * xpitch;
+      if (p.kc <= 256) {
+        if (lane == 0)
+          for (int r0 = 0, left = groups * 8; left > 0;) {
+            const int h = left >= 64 ? 64 : left >= 32 ? 32 : left >= 16 ? 16 : 8;
+            const CUtensorMap* map = h == 64   ? &p.tmap_a_rows[0]
+                                     : h == 32 ? &p.tmap_a_rows[1]
+                                     : h == 16 ? &p.tmap_a_rows[2]
+                                               : &p.tmap_a;
+            tma_load_2d(abase + r0 * bw * 2, map, k0, row0 + r0, &full[stage]);
+            r0 += h;
+            left -= h;
+          }
+      } else {
+        for (int i = lane; i < groups * boxes; i += 32) {
+          const int grp = i / boxes, box = i - grp * boxes;
+          tma_load_2d(abase + (grp * (p.kc / bw) + box) * (8 * bw * 2), &p.tmap_a, k0 + box * bw,
+                      row0 + grp * 8, &full[stage]);
+        }
+      }
+    }
+    __syncwarp();
+    cluster_arrive();  // #1: the producer takes no part in the z sum
+    // Expand stages: consecutive 128-column units merged while B rows fit p.bstage.
+    for (int u = u0; u < u1 && alive;) {
+      const int cb = u;
+      const int max_cols = min(kStageCols, p.bstage / (2 * si.bucket));  // >= kExpandCols
+      const int take = min(max_cols / kExpandCols, u1 - u);
+      const int cc0 = cb * kExpandCols;
+      const int nc = min(p.N, (cb + take) * kExpandCols) - cc0;
+      u += take;
+      const int stage = ring.stage;
+      const uint32_t phase = ring.phase;
+      ring.next(NS);
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait(&empty[stage], phase ^ 1u) ? 1 : 0;
+      if (!__shfl_sync(0xffffffffu, ok, 0)) {
+        alive = false;
+        break;
+      }
+      uint8_t* st = smem + stage * SB;
+      ExpandHeader* h = reinterpret_cast<ExpandHeader*>(st + hoff);
+      if (lane == 0) {
+        const int s0 = slice_of(offs, p.S, cc0), s1 = slice_of(offs, p.S, cc0 + nc - 1);
+        h->ok = 1;
+        h->seg = seg;
+        h->n = si.n;
+        h->r = si.r;
+        h->bucket = si.bucket;
+        h->pos0 = si.pos0;
+        h->col0 = cc0;
+        h->ncols = nc;
+        h->slice = s0 == s1 ? s0 : -1;
+        h->scale = si.scale;
+      }
+      if (lane < kSeg) h->tok[lane] = tok;
+      const uint16_t* bsrc = p.b + si.boff + int64_t(cc0) * si.bucket;
+      const uint32_t bbytes = uint32_t(nc) * si.bucket * 2;
+      const uint32_t bbulk = bbytes & ~15u;
+      for (uint32_t i = bbulk / 2 + lane; i < bbytes / 2; i += 32)
+        reinterpret_cast<uint16_t*>(st)[i] = bsrc[i];
+      const uint32_t ybytes = STAGED ? uint32_t(nc) * 2 : 0u;
+      __syncwarp();
+      if (lane == 0) mbar_arrive_expect_tx(&full[stage], bbulk + uint32_t(si.n) * ybytes);
+      __syncwarp();
+      if (lane == 31 && bbulk) bulk_g2s(st, bsrc, bbulk, &full[stage]);
+      if (STAGED && lane < si.n)
+        bulk_g2s(st + p.bstage + lane * kYStagePitch, p.y + int64_t(tok) * p.y_stride + cc0, ybytes,
+                 &full[stage]);
+    }
+    if (alive) {  // end of stream
+      const int stage = ring.stage;
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait(&empty[stage], ring.phase ^ 1u) ? 1 : 0;
+      if (__shfl_sync(0xffffffffu, ok, 0) && lane == 0) {
+        reinterpret_cast<ExpandHeader*>(smem + stage * SB + hoff)->ok = -1;
+        mbar_arrive(&full[stage]);
+      }
+    }
+    __syncwarp();
+    cluster_wait();  // #1
+    cluster_arrive();
+    cluster_wait();  // #2
+    return;
+  }
+
+  // -------------------------------------------------------------- consumer warps
+  const int g = lane >> 2, t = lane & 3;
+  const int ntiles = (R + 7) >> 3;  // 1..8 (S*r <= 64)
+  const int kparts = kConsumerWarps / ntiles;
+  const int tile = warp / kparts, kpart = warp - tile * kparts;
+  float d[4] = {0.f, 0.f, 0.f, 0.f};
+  bool aborted = false;
+  Ring ring;
+  for (int c = c0; c < c1; ++c, ring.next(NS)) {
+    const int stage = ring.stage;
+    if (!mbar_wait(&full[stage], ring.phase)) {
+      aborted = true;
+      break;
+    }
+    const uint8_t* st = smem + stage * SB;
+    const int len = min(p.kc, p.K - c * p.kc);
+    if (tile < ntiles) shrink_unit_regs(st, xpitch, p.kc, len, tile, kpart, kparts, g, t, d);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[stage]);
+  }
+  aborted = !consumers_all(!aborted);
+  // This CTA's part of z: warps of one n tile hold interleaved k blocks; add them in
+  // warp order.  Rows past the segment's tokens are never read.
+  float* rw = red + warp * kSeg * 8;
+  *reinterpret_cast<float2*>(rw + g * 8 + 2 * t) = make_float2(d[0], d[1]);
+  *reinterpret_cast<float2*>(rw + (g + 8) * 8 + 2 * t) = make_float2(d[2], d[3]);
+  consumers_sync();
+  for (int e = tid; e < kSeg * kZsPitch; e += kConsumers) {
+    const int m = e / kZsPitch, j = e - m * kZsPitch;
+    float s = 0.f;
+    if (j < R)
+      for (int k = 0; k < kparts; ++k) s += red[(((j >> 3) * kparts + k) * kSeg + m) * 8 + (j & 7)];
+    zpart[e] = s;
+  }
+  cluster_arrive();
+  cluster_wait();  // #1: every CTA's partial is written
+  for (int e = tid; e < kSeg * kZsPitch; e += kConsumers) {
+    float s = 0.f;
+    for (int r = 0; r < C; ++r) s += cluster.map_shared_rank(zpart, r)[e];
+    zs[e] = s;
+  }
+  consumers_sync();
+  if (!aborted) {
+    uint32_t zf[4][2][4];
+    int zseg = -1, zslice = -1;
+    for (;; ring.next(NS)) {
+      const int stage = ring.stage;
+      if (!mbar_wait(&full[stage], ring.phase)) break;
+      const uint8_t* st = smem + stage * SB;
+      const ExpandHeader& h = *reinterpret_cast<const ExpandHeader*>(st + hoff);
+      if (h.ok < 0) break;
+      if (STAGED && h.slice >= 0 && h.bucket <= 16) {
+        if (h.bucket == 16) expand_stage_pair<16, MODE, true>(p, h, st, zf, zseg, zslice, lane, warp, zs);
+        else expand_stage_pair<8, MODE, true>(p, h, st, zf, zseg, zslice, lane, warp, zs);
+      } else switch (h.bucket < 8 ? 8 : h.bucket) {
+        case 8: expand_stage<8, MODE, STAGED, true>(p, h, st, offs, zf, zseg, zslice, lane, warp, zs); break;
+        case 16: expand_stage<16, MODE, STAGED, true>(p, h, st, offs, zf, zseg, zslice, lane, warp, zs); break;
+        case 32: expand_stage<32, MODE, STAGED, true>(p, h, st, offs, zf, zseg, zslice, lane, warp, zs); break;
+        default: expand_stage<64, MODE, STAGED, true>(p, h, st, offs, zf, zseg, zslice, lane, warp, zs); break;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[stage]);
+    }
+  }
+  cluster_arrive();
+  cluster_wait();  // #2: no peer reads this CTA's partial any more
+}
+
 // ====================================================================== host side
 struct ShrinkConfig {
   int rstride, kc, nchunks, stages, stage_bytes, smem;
@@ -1140,6 +1408,54 @@ inline ExpandConfig expand_config(bool staged, int bstage) {
   int stages = kStageBudget / c.stage_bytes;
   c.stages = stages < 2 ? 2 : (stages > kMaxStages ? kMaxStages : stages);
   c.smem = c.stages * c.stage_bytes + 2 * kMaxStages * 8 + (kMaxSlices + 4) * 4;
+  return c;
+}
+
+// The one-launch kernel (sgmv_cluster_kernel): the register path only (S*r <= 64); one
+// stage size for both phases (the larger of a shrink stage and an expand stage), at least
+// two stages in the two-CTA budget; the widest K chunk that allows that.  Cluster size C:
+// the segment's A and B bytes (at the capacity's rank and bucket) over 256 KiB, rounded up
+// to a power of two, at most 8.  Taken only when a segment's B rows are no more bytes than
+// its A rows: BASELINE config 1 measured qkv 31.6 -> 29.7 us and down 29.2 -> 29.7 us with
+// it, but gate_up (B 3.5x A) 48.1 -> 73.8 us, its expand spread over a cluster per segment
+// in two waves instead of the persistent expand's balanced split.
+struct ClusterConfig {
+  bool ok;
+  int C, kc, nchunks, stages, stage_bytes, smem;
+};
+
+inline ClusterConfig cluster_config(int64_t width, int out_width, int num_slices, int capacity,
+                                    bool staged, int bstage) {
+  ClusterConfig c{};
+  const int cap = capacity < kMaxRank ? capacity : kMaxRank;
+  const int rstride = round_up(num_slices * cap, 8);
+  if (rstride > 64) return c;
+  const int fixed = kConsumerWarps * kSeg * 8 * 4 + 2 * kSeg * kZsPitch * 4 + 2 * kMaxStages * 8 +
+                    (kMaxSlices + 4) * 4;
+  const int ebytes = round_up(bstage + (staged ? kSeg * kYStagePitch : 0) + kHeaderBytes, 128);
+  int kc = 0;
+  for (int cand : {512, 256, 128, 64}) {
+    const int sb = std::max(shrink_stage_bytes(rstride, cand), ebytes);
+    if (2 * sb + fixed <= kStageBudget) {
+      kc = cand;
+      break;
+    }
+  }
+  if (kc == 0) return c;
+  while (kc > 64 && kc / 2 >= width) kc /= 2;
+  c.kc = kc;
+  c.nchunks = int((width + kc - 1) / kc);
+  c.stage_bytes = std::max(shrink_stage_bytes(rstride, kc), ebytes);
+  const int stages = (kStageBudget - fixed) / c.stage_bytes;
+  c.stages = stages > kMaxStages ? kMaxStages : stages;
+  c.smem = c.stages * c.stage_bytes + fixed;
+  int bucket = 1;
+  while (bucket < cap) bucket *= 2;
+  const int64_t seg_bytes = int64_t(rstride) * width * 2 + int64_t(out_width) * bucket * 2;
+  int C = 1;
+  while (C < 8 && seg_bytes > int64_t(C) * 256 * 1024) C *= 2;
+  c.C = C;
+  c.ok = int64_t(out_width) * bucket <= int64_t(rstride) * width;
   return c;
 }
 
@@ -1312,13 +1628,20 @@ int fused_launch(const void* x, int64_t x_stride, const void* a, const void* b,
            segment_count, scratch.data, scratch.data + int64_t(sc.nchunks) * T * sc.rstride,
            scratch.counters, int(T), int(width), out_width, num_slices, capacity, num_slots, max_segments,
            sc.rstride, sc.kc, sc.nchunks, sc.stages, sc.stage_bytes, max_tokens};
+  // Both phases in one call and the register path: one launch, z in shared memory.
+  const ClusterConfig cc = cluster_config(width, out_width, num_slices, capacity, staged, bstage);
+  const bool one_launch = phases == (kPhaseShrink | kPhaseExpand) && cc.ok;
+  if (one_launch) {
+    p.kc = cc.kc;
+    p.nchunks = cc.nchunks;
+  }
   {
     // A as a 2-D tensor [num_slots*S*cap rows, K columns] for the shrink's TMA boxes.
     const PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
     if (!encode) return fail(LF_E_CUDA, "fused_shrink_expand: cuTensorMapEncodeTiled unavailable");
     const cuuint64_t dims[2] = {cuuint64_t(width), cuuint64_t(num_slots) * num_slices * capacity};
     const cuuint64_t strides[1] = {cuuint64_t(width) * 2};
-    const cuuint32_t box[2] = {cuuint32_t(sc.kc < 256 ? sc.kc : 256), 8};
+    const cuuint32_t box[2] = {cuuint32_t(p.kc < 256 ? p.kc : 256), 8};
     const cuuint32_t estr[2] = {1, 1};
     CUresult r = encode(&p.tmap_a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(a), dims, strides, box,
                         estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -1340,6 +1663,38 @@ int fused_launch(const void* x, int64_t x_stride, const void* a, const void* b,
   if (seg_cap * sc.nchunks >= (int64_t(1) << 31) ||
       seg_cap * ((out_width + kExpandCols - 1) / kExpandCols) >= (int64_t(1) << 31))
     return fail(LF_E_INVALID, "fused_shrink_expand: too many (segment, chunk) units");
+  if (one_launch) {
+    p.stages = cc.stages;
+    p.stage_bytes = cc.stage_bytes;
+    p.bstage = bstage;
+    auto kernel = numerics == kFp32
+                      ? (staged ? sgmv_cluster_kernel<kFp32, true> : sgmv_cluster_kernel<kFp32, false>)
+                      : (staged ? sgmv_cluster_kernel<kReference, true>
+                                : sgmv_cluster_kernel<kReference, false>);
+    static int flags[4][64] = {};
+    if (int rc = ensure_smem(kernel, cc.smem, flags[numerics * 2 + (staged ? 1 : 0)])) return rc;
+    if (seg_cap * cc.C >= (int64_t(1) << 31)) return fail(LF_E_INVALID, "fused_shrink_expand: too many segments");
+    cudaLaunchConfig_t config = {};
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = unsigned(cc.C);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    config.attrs = attr;
+    config.numAttrs = 2;
+    config.gridDim = dim3(unsigned(seg_cap * cc.C));
+    config.blockDim = dim3(kThreads);
+    config.dynamicSmemBytes = cc.smem;
+    config.stream = s;
+    const cudaError_t err = cudaLaunchKernelEx(&config, kernel, p);
+    if (err != cudaSuccess) {
+      last_error() = std::string("fused_shrink_expand (one launch): ") + cudaGetErrorString(err);
+      return LF_E_CUDA;
+    }
+    return LF_OK;
+  }
   if (phases & kPhaseShrink) {
     // Up to 8 n tiles (S*r <= 64) the warps accumulate in registers.
     const bool regs = sc.rstride <= 64;

@@ -14,7 +14,7 @@ from golden_io import bf16_bits, rel_l2  # noqa: E402
 from oracle import cpu_reference as ref  # noqa: E402
 
 from loraforge_b200.ops import row_expand, row_shrink  # noqa: E402
-from loraforge_b200.ops.fused import lora_shrink_expand  # noqa: E402
+from loraforge_b200.ops.fused import lora_shrink_expand, sgmv_expand, sgmv_shrink, workspace_floats  # noqa: E402
 from loraforge_b200.ops.grouping import group_tokens  # noqa: E402
 
 ROUTING_KEYS = ("segment_indptr", "segment_slots", "token_indices", "segment_count")
@@ -127,6 +127,32 @@ def test_reference_numerics_on_golden_cases(slices):
     routes_np = gold["routes"]
     skipped = (routes_np == -1) | (routes_np == 8)
     np.testing.assert_array_equal(bf16_bits(out)[skipped], bf16_bits(before)[skipped])
+
+
+@pytest.mark.parametrize("numerics", ["fp32", "reference"])
+@pytest.mark.parametrize(
+    "k,widths,rank",
+    [(1024, (1024,), 16), (8192, (4096,), 16), (4096, (4096, 1024, 1024), 16), (30720, (4096,), 16)],
+)
+def test_one_launch_cluster_sizes(k, widths, rank, numerics):
+    """A whole call whose B rows are no more bytes than its A rows runs as one launch with z in
+    shared memory, one thread-block cluster of 1, 2, 4 or 8 CTAs per segment (these four
+    shapes).  Against the FP32 oracle, and against the same call as two launches (split-K
+    shrink into the workspace, then expand), which adds z's K parts in another order."""
+    x, a, b, base, slots_t, meta, S, cap = decode_case(k=k, widths=widths, ranks=[rank] * 24, seed=31)
+    one = fused(x, a, b, base.clone(), meta, S, numerics=numerics)
+    again = fused(x, a, b, base.clone(), meta, S, numerics=numerics)
+    assert torch.equal(one, again)  # deterministic
+    ws = torch.zeros(workspace_floats(x.shape[0], k, S, cap), dtype=torch.float32, device="cuda")
+    two = base.clone()
+    sgmv_shrink(x, a, b, two, workspace=ws, **meta, num_slices=S, numerics=numerics)
+    sgmv_expand(x, a, b, two, workspace=ws, **meta, num_slices=S, numerics=numerics)
+    torch.cuda.synchronize()
+    assert np.mean(bf16_bits(one) == bf16_bits(two)) > 0.98
+    if numerics == "fp32":
+        gate = ref.fp32_gate(values(bf16_bits(one)), fp32_reference(x, a, b, base, slots_t, meta, S))
+        assert gate["excess"] <= 1e-2, gate
+        assert gate["exact"] > 0.99, gate
 
 
 def test_reference_numerics_match_decomposed_operators():

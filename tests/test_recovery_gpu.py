@@ -28,6 +28,8 @@ from test_fused_gpu import decode_case  # noqa: E402
 from loraforge_b200 import _native  # noqa: E402
 from loraforge_b200.ops.fused import (  # noqa: E402
     lora_shrink_expand,
+    sgmv_expand,
+    sgmv_shrink,
     reset_builtin_workspace,
     reset_workspace,
     workspace_floats,
@@ -99,12 +101,20 @@ def test_peer_all_reduce_raises_on_expiry(monkeypatch):
         peer.close()
 
 
+def _two_launches(x, a, b, y, meta, S, ws):
+    # The split-K shrink and the expand as two launches on one workspace: the path whose
+    # per-segment completion counters live in the workspace (row-parallel calls take it; a
+    # whole lora_shrink_expand call of rank <= 64 runs as one launch without a workspace).
+    sgmv_shrink(x, a, b, y, workspace=ws, **meta, num_slices=S)
+    sgmv_expand(x, a, b, y, workspace=ws, **meta, num_slices=S)
+
+
 def test_overwritten_workspace_counters_are_restored_by_reset():
     x, a, b, base, slots_t, meta, S, cap = decode_case(seed=21, widths=(14336, 14336))
     T, K = x.shape
     fresh = torch.zeros(workspace_floats(T, K, S, cap), dtype=torch.float32, device="cuda")
     want = base.clone()
-    lora_shrink_expand(x, a, b, want, **meta, num_slices=S, workspace=fresh)
+    _two_launches(x, a, b, want, meta, S, fresh)
     ws = torch.zeros_like(fresh)
     offset = z_rows(ws, T, K, S, cap).data_ptr() // 4 - ws.data_ptr() // 4
     row = z_rows(ws, T, K, S, cap).shape[1]
@@ -112,13 +122,13 @@ def test_overwritten_workspace_counters_are_restored_by_reset():
     counters.fill_(3)  # foreign values where the per-segment counters live
     reset_workspace(ws, T, K, S, cap)
     got = base.clone()
-    lora_shrink_expand(x, a, b, got, **meta, num_slices=S, workspace=ws)
+    _two_launches(x, a, b, got, meta, S, ws)
     torch.cuda.synchronize()
     assert torch.equal(got, want)
     assert int(counters.abs().sum()) == 0
     # And again on the same workspace: every call leaves the counters at zero.
     again = base.clone()
-    lora_shrink_expand(x, a, b, again, **meta, num_slices=S, workspace=ws)
+    _two_launches(x, a, b, again, meta, S, ws)
     torch.cuda.synchronize()
     assert torch.equal(again, want)
 

@@ -85,13 +85,26 @@ def test_row_parallel_two_shards_with_z_sum():
     assert gate["excess"] <= 1e-2, gate
 
 
-def test_split_halves_equal_fused_call():
+def test_split_halves_agree_with_fused_call():
+    """The two halves (shrink, then expand on the same workspace; the row-parallel path) compute
+    what one fused call computes.  The fused call runs the one-launch kernel, which adds z's K
+    parts in another order, so the two agree within the FP32 gate and on almost every output
+    bit rather than bit for bit; each is deterministic."""
     x, a, b, base, slots_t, meta, S, cap = decode_case(tokens=64, slots=12, seed=13)
-    fused = base.clone()
-    lora_shrink_expand(x, a, b, fused, **meta, num_slices=S)
-    ws = torch.zeros(workspace_floats(x.shape[0], x.shape[1], S, cap), dtype=torch.float32, device="cuda")
-    split = base.clone()
-    sgmv_shrink(x, a, b, split, workspace=ws, **meta, num_slices=S)
-    sgmv_expand(x, a, b, split, workspace=ws, **meta, num_slices=S)
-    torch.cuda.synchronize()
-    assert torch.equal(split, fused)
+    expected = fp32_reference(x, a, b, base, slots_t, meta, S)
+    outs = []
+    for _ in range(2):
+        fused = base.clone()
+        lora_shrink_expand(x, a, b, fused, **meta, num_slices=S)
+        ws = torch.zeros(workspace_floats(x.shape[0], x.shape[1], S, cap), dtype=torch.float32, device="cuda")
+        split = base.clone()
+        sgmv_shrink(x, a, b, split, workspace=ws, **meta, num_slices=S)
+        sgmv_expand(x, a, b, split, workspace=ws, **meta, num_slices=S)
+        torch.cuda.synchronize()
+        outs.append((fused, split))
+    (fused, split), (fused2, split2) = outs
+    assert torch.equal(fused, fused2) and torch.equal(split, split2)
+    for out in (fused, split):
+        gate = ref.fp32_gate(values(bf16_bits(out)), expected)
+        assert gate["excess"] <= 1e-2, gate
+    assert np.mean(bf16_bits(split) == bf16_bits(fused)) > 0.99
