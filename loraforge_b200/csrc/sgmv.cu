@@ -764,7 +764,7 @@ __device__ __forceinline__ void expand_stage(const Params& p, const ExpandHeader
   }
 }
 
-// Stages whose columns lie in one slice, with y staged and bucket <= 16: each warp runs
+// Stages whose columns lie in one slice, with y staged and bucket <= 32: each warp runs
 // two of its 32-column groups side by side (same arithmetic as expand_stage), so the y
 // loads, MMA chains and stores of one group overlap the latencies of the other.
 template <int KP, int MODE, bool ZS = false>
@@ -816,8 +816,10 @@ __device__ __forceinline__ void expand_stage_pair(const Params& p, const ExpandH
           if constexpr (KP == 8) {
             mma1688(d[q][j], zf[0][part][0], zf[0][part][1], bf[0][0]);
           } else {
-            mma16816(d[q][j], zf[0][part][0], zf[0][part][1], zf[0][part][2], zf[0][part][3], bf[0][0],
-                     bf[0][1]);
+#pragma unroll
+            for (int k16 = 0; k16 < KP / 16; ++k16)
+              mma16816(d[q][j], zf[k16][part][0], zf[k16][part][1], zf[k16][part][2], zf[k16][part][3],
+                       bf[k16][0], bf[k16][1]);
           }
         }
       }
@@ -1063,8 +1065,9 @@ __global__ void __launch_bounds__(kThreads, 2) sgmv_expand_kernel(const __grid_c
     const uint8_t* st = smem + stage * SB;
     const ExpandHeader& h = *reinterpret_cast<const ExpandHeader*>(st + hoff);
     if (h.ok < 0) break;
-    if (STAGED && h.slice >= 0 && h.bucket <= 16) {
-      if (h.bucket == 16) expand_stage_pair<16, MODE>(p, h, st, zf, zseg, zslice, lane, warp);
+    if (STAGED && h.slice >= 0 && h.bucket <= 32) {
+      if (h.bucket == 32) expand_stage_pair<32, MODE>(p, h, st, zf, zseg, zslice, lane, warp);
+      else if (h.bucket == 16) expand_stage_pair<16, MODE>(p, h, st, zf, zseg, zslice, lane, warp);
       else expand_stage_pair<8, MODE>(p, h, st, zf, zseg, zslice, lane, warp);
     } else switch (h.bucket < 8 ? 8 : h.bucket) {
       case 8: expand_stage<8, MODE, STAGED>(p, h, st, offs, zf, zseg, zslice, lane, warp); break;
@@ -1317,8 +1320,9 @@ __global__ void __launch_bounds__(kThreads, 2) sgmv_cluster_kernel(const __grid_
       const uint8_t* st = smem + stage * SB;
       const ExpandHeader& h = *reinterpret_cast<const ExpandHeader*>(st + hoff);
       if (h.ok < 0) break;
-      if (STAGED && h.slice >= 0 && h.bucket <= 16) {
-        if (h.bucket == 16) expand_stage_pair<16, MODE, true>(p, h, st, zf, zseg, zslice, lane, warp, zs);
+      if (STAGED && h.slice >= 0 && h.bucket <= 32) {
+        if (h.bucket == 32) expand_stage_pair<32, MODE, true>(p, h, st, zf, zseg, zslice, lane, warp, zs);
+        else if (h.bucket == 16) expand_stage_pair<16, MODE, true>(p, h, st, zf, zseg, zslice, lane, warp, zs);
         else expand_stage_pair<8, MODE, true>(p, h, st, zf, zseg, zslice, lane, warp, zs);
       } else switch (h.bucket < 8 ? 8 : h.bucket) {
         case 8: expand_stage<8, MODE, STAGED, true>(p, h, st, offs, zf, zseg, zslice, lane, warp, zs); break;
