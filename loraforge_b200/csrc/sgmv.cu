@@ -764,9 +764,11 @@ __device__ __forceinline__ void expand_stage(const Params& p, const ExpandHeader
   }
 }
 
-// Stages whose columns lie in one slice, with y staged and bucket <= 32: each warp runs
-// two of its 32-column groups side by side (same arithmetic as expand_stage), so the y
-// loads, MMA chains and stores of one group overlap the latencies of the other.
+// Stages whose columns lie in one slice, with y staged: each warp runs two of its
+// 32-column groups side by side (same arithmetic as expand_stage), so the y loads, MMA
+// chains and stores of one group overlap the latencies of the other.  Measured per bucket:
+// 16 (config 1, where it was introduced), 32 (config 4 365 -> 360 us/step) and 64
+// (config 2 68.8 -> 66.1).
 template <int KP, int MODE, bool ZS = false>
 __device__ __forceinline__ void expand_stage_pair(const Params& p, const ExpandHeader& h,
                                                   const uint8_t* st, uint32_t (&zf)[4][2][4],
@@ -1065,8 +1067,9 @@ __global__ void __launch_bounds__(kThreads, 2) sgmv_expand_kernel(const __grid_c
     const uint8_t* st = smem + stage * SB;
     const ExpandHeader& h = *reinterpret_cast<const ExpandHeader*>(st + hoff);
     if (h.ok < 0) break;
-    if (STAGED && h.slice >= 0 && h.bucket <= 32) {
-      if (h.bucket == 32) expand_stage_pair<32, MODE>(p, h, st, zf, zseg, zslice, lane, warp);
+    if (STAGED && h.slice >= 0) {
+      if (h.bucket == 64) expand_stage_pair<64, MODE>(p, h, st, zf, zseg, zslice, lane, warp);
+      else if (h.bucket == 32) expand_stage_pair<32, MODE>(p, h, st, zf, zseg, zslice, lane, warp);
       else if (h.bucket == 16) expand_stage_pair<16, MODE>(p, h, st, zf, zseg, zslice, lane, warp);
       else expand_stage_pair<8, MODE>(p, h, st, zf, zseg, zslice, lane, warp);
     } else switch (h.bucket < 8 ? 8 : h.bucket) {
@@ -1320,8 +1323,9 @@ __global__ void __launch_bounds__(kThreads, 2) sgmv_cluster_kernel(const __grid_
       const uint8_t* st = smem + stage * SB;
       const ExpandHeader& h = *reinterpret_cast<const ExpandHeader*>(st + hoff);
       if (h.ok < 0) break;
-      if (STAGED && h.slice >= 0 && h.bucket <= 32) {
-        if (h.bucket == 32) expand_stage_pair<32, MODE, true>(p, h, st, zf, zseg, zslice, lane, warp, zs);
+      if (STAGED && h.slice >= 0) {
+        if (h.bucket == 64) expand_stage_pair<64, MODE, true>(p, h, st, zf, zseg, zslice, lane, warp, zs);
+        else if (h.bucket == 32) expand_stage_pair<32, MODE, true>(p, h, st, zf, zseg, zslice, lane, warp, zs);
         else if (h.bucket == 16) expand_stage_pair<16, MODE, true>(p, h, st, zf, zseg, zslice, lane, warp, zs);
         else expand_stage_pair<8, MODE, true>(p, h, st, zf, zseg, zslice, lane, warp, zs);
       } else switch (h.bucket < 8 ? 8 : h.bucket) {
