@@ -57,9 +57,9 @@ L2_NOTE = "flushed before every timed step (256 MiB write, outside the step even
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of the dominant
 # call, from one ncu capture per (config, path, call); the commands are in profiles/.
 TRAFFIC = {
-    (1, "fused", "gate_up_proj.fused"): (19.430144 + 75.358720 + 3.842816) * 1e6,
-    (2, "fused", "proj.fused"): (51.121664 + 0.143360 + 49.703424 + 0.023040) * 1e6,
-    (4, "fused", "gate_up_proj.fused"): (145.522688 + 3.292672 + 822.391040 + 51.766784) * 1e6,
+    (1, "fused", "gate_up_proj.fused"): (19.434496 + 75.373056 + 0.404224) * 1e6,
+    (2, "fused", "proj.fused"): (51.122176 + 0.006656 + 49.678592 + 0.019456) * 1e6,
+    (4, "fused", "gate_up_proj.fused"): (145.565696 + 0.168192 + 820.420352 + 53.785344) * 1e6,
 }
 
 
