@@ -1,7 +1,7 @@
 """Multi-LoRA shrink+expand benchmark (BASELINE.json metric) on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config 1|2|3|4] [--path fused|rows] [--no-sub]
+                    [--config 1|2|3|4] [--path fused|rows|bgmv|vllm|base_gemm|base_cublas] [--no-sub]
 
 Default workload: BASELINE config 4, the configuration the metric's "1/2/4/8 B200" clause
 is quoted on: one decode batch of 512 tokens over 1024 resident rank-32 adapters (ids
@@ -13,8 +13,10 @@ routes the same seeded batch and holds its shard of one seeded global weight set
 
 At N=1 the line also carries ``sub``: configs 1 (Llama-3-8B decode, 256 tokens, 128
 rank-16 adapters), 2 (retained-rank compact B, ranks U{4..64}) and 3 (8192-token prefill
-in geometric segments, rank 64), the row-operator pair on config 1, and the reference's own
-CUDA row kernels on config 1 (built for sm_100a into oracle/_ref: the bar on the same box),
+in geometric segments, rank 64), the row-operator pair on config 1, the padded SGLang BGMV
+pair (lora_shrink / lora_expand) and the vLLM BGMV pair (vllm_gemv.shrink / expand) on config 1,
+and the reference's own CUDA row kernels on config 1 (built for sm_100a into oracle/_ref: the
+bar on the same box),
 and on config 3 the base projection with the LoRA delta in one GEMM (lora_base_gemm) next to
 cuBLAS's base GEMM followed by lora_shrink_expand_prefill, each timed the same way with its
 own roofline, e2e, CPU baseline and output check.
@@ -52,6 +54,9 @@ import numpy as np
 
 ROOT = Path(__file__).resolve().parent
 METRIC = "multi-LoRA shrink+expand tokens/s"
+# Paths that round z (and the scaled delta) to BF16, held to the reference's gate for its row
+# operators (relative L2 < 0.005) instead of BASELINE's FP32 gate.
+ROUNDED_Z_PATHS = ("rows", "reference_cuda", "bgmv")
 L2_NOTE = "flushed before every timed step (256 MiB write, outside the step events)"
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of the dominant
@@ -71,7 +76,8 @@ def parse_args(argv=None):
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--config", type=int, choices=(1, 2, 3, 4), default=4)
     p.add_argument("--seed", type=int, default=1234)
-    p.add_argument("--path", choices=("fused", "rows", "base_gemm", "base_cublas"), default="fused")
+    p.add_argument("--path", choices=("fused", "rows", "bgmv", "vllm", "base_gemm", "base_cublas"),
+                   default="fused")
     p.add_argument("--allreduce", choices=("peer", "nccl"), default="peer",
                    help="tensor-parallel z sum: one kernel over NVLink peer memory, or NCCL")
     p.add_argument("--no-sub", action="store_true", help="skip the config 1-3 sub-records")
@@ -325,6 +331,20 @@ class Workload:
                 p.w.mul_(p.K**-0.5)
                 p.gemm_ws = torch.zeros(base_gemm_workspace_floats(self.T, p.K, p.S, p.cap), dtype=torch.float32,
                                         device=device)
+        if path in ("bgmv", "vllm"):
+            # The padded BGMV layouts: B as [slots, N, capacity] (the compact store when every
+            # slot's bucket is the capacity) and, for vLLM, per-slice views of A and B.
+            for p in self.projections:
+                G = self.nslots
+                if not (p.buckets_np == p.cap).all() or not (self.ranks_np == p.cap).all():
+                    raise ValueError(f"--path {path} needs every slot at the full rank capacity")
+                p.b_pad = p.b[: G * p.N * p.cap].view(G, p.N, p.cap)
+                cols = np.cumsum((0, *p.widths))
+                p.a_slices = [p.a[:, s * p.cap : (s + 1) * p.cap, :] for s in range(p.S)]
+                p.b_slices = [p.b_pad[:, int(cols[s]) : int(cols[s + 1]), :] for s in range(p.S)]
+                p.v = torch.zeros(p.S, self.T, p.cap, dtype=torch.float32, device=device)
+            if path == "vllm" and len(set(self.scales_np.tolist())) != 1:
+                raise ValueError("--path vllm takes one scale for every slot")
         self.slots = torch.from_numpy(self.slots_np).to(device)
         self.routing = empty_routing(self.T, device)
         self.peer = None
@@ -348,13 +368,16 @@ def run_step(w, mark=None):
     ``w.path == "fused"``: lora_shrink_expand per projection (prefill configs:
     lora_shrink_expand_prefill over segments of up to 128 tokens on the tcgen05 tiles);
     ``"rows"``: row_shrink + row_expand per projection (the reference's operator pair);
+    ``"bgmv"``: lora_shrink + lora_expand per projection (the padded SGLang BGMV operators, B as
+    [slots, N, capacity]); ``"vllm"``: vllm_gemv.shrink + expand per projection (vLLM's
+    per-slice padded tensors, FP32 intermediate);
     ``"reference_cuda"``: the same pair run by the reference's own CUDA kernels, built for
     sm_100a into oracle/_ref (a comparison bar on the same box, never this repository's path);
     tensor-parallel configs: gate/up column-parallel, down as shrink, sum of the z rows
     over the ranks, expand.  ``mark(label)``, when given, records a CUDA event that starts
     the interval named `label` (ended by the next mark or "end").
     """
-    from loraforge_b200.ops import row_expand, row_shrink
+    from loraforge_b200.ops import lora_expand, lora_shrink, row_expand, row_shrink, vllm_gemv
     from loraforge_b200.ops.fused import (
         lora_base_gemm,
         lora_shrink_expand,
@@ -411,6 +434,16 @@ def run_step(w, mark=None):
             w.ref.expand(p.z, p.b, p.b_offsets, p.b_strides, p.y, r.segment_indptr, r.segment_slots,
                          r.token_indices, p.ranks, p.scales, p.slice_offsets, r.segment_count, p.N, p.cap,
                          2 * w.sms, 256)
+        elif w.path == "bgmv":
+            mark(f"{p.name}.shrink")
+            z = lora_shrink(x, p.a, p.ranks, w.slots, num_slices=p.S)
+            mark(f"{p.name}.expand")
+            lora_expand(z, p.b_pad, p.ranks, p.scales, w.slots, p.slice_offsets, max(p.widths), base=p.y)
+        elif w.path == "vllm":
+            mark(f"{p.name}.shrink")
+            vllm_gemv.shrink(x, p.a_slices, p.v, w.slots, scale=float(w.scales_np[0]))
+            mark(f"{p.name}.expand")
+            vllm_gemv.expand(p.v, p.b_slices, p.y, w.slots, offset=0, add=True)
         else:
             mark(f"{p.name}.shrink")
             row_shrink(x, p.a, p.z, w.slots, p.ranks, num_slices=p.S, max_rank=p.cap)
@@ -473,7 +506,7 @@ def check_outputs(w):
         gate["rel_l2"] = float(np.linalg.norm(got - expected) / max(np.linalg.norm(expected), 1e-30))
         worst = {"excess": max(worst["excess"], gate["excess"]), "raw": max(worst["raw"], gate["raw"]),
                  "exact": min(worst["exact"], gate["exact"]), "rel_l2": max(worst["rel_l2"], gate["rel_l2"])}
-    ok = worst["rel_l2"] < 0.005 if w.path in ("rows", "reference_cuda") else worst["excess"] <= 1e-2
+    ok = worst["rel_l2"] < 0.005 if w.path in ROUNDED_Z_PATHS else worst["excess"] <= 1e-2
     return ok, worst
 
 
@@ -764,7 +797,7 @@ def measure(config, args, world, rank, local, path="fused", sub=False):
         ok, gate = check_outputs(w)
         ok = reduce_over_ranks(1.0 if ok else 0.0, world, op="min") == 1.0
         record["check"] = {"result": "pass" if ok else "fail",
-                           "gate": ("relative L2 < 0.005 vs FP32 oracle" if path in ("rows", "reference_cuda") else
+                           "gate": ("relative L2 < 0.005 vs FP32 oracle" if path in ROUNDED_Z_PATHS else
                                     "max|out-ref| beyond BF16 rounding <= 1e-2 RMS vs FP32 oracle"),
                            "excess": reduce_over_ranks(gate["excess"], world),
                            "raw": reduce_over_ranks(gate["raw"], world),
@@ -835,7 +868,7 @@ def measure(config, args, world, rank, local, path="fused", sub=False):
     if "down_proj.allreduce" in per_kernel:  # the z sum, timed on its own
         record["allreduce_us"] = reduce_over_ranks(per_kernel["down_proj.allreduce"], world) * 1e3
     if (rank == 0 and world == 1 and not args.no_cpu_baseline and not args.profile
-            and path not in ("reference_cuda", "base_gemm", "base_cublas")):
+            and path not in ("reference_cuda", "bgmv", "vllm", "base_gemm", "base_cublas")):
         record["cpu_baseline"] = cpu_baseline(host, budget_s=8.0 if sub else 12.0)
     if path == "reference_cuda":
         record["impl"] = "reference CUDA kernels (src/loraforge/ops/csrc/lora_rows.cu, sm_100a, oracle/_ref)"
@@ -876,7 +909,7 @@ def main(argv=None):
     if world == 1 and args.config == 4 and not args.no_sub and not args.profile:
         sub = {}
         for config, path in ((1, "fused"), (2, "fused"), (3, "fused"), (1, "rows"), (1, "reference_cuda"),
-                             (3, "base_gemm"), (3, "base_cublas")):
+                             (1, "bgmv"), (1, "vllm"), (3, "base_gemm"), (3, "base_cublas")):
             rec = measure(config, args, world, rank, local, path, sub=True)
             sub[f"config{config}" + ("" if path == "fused" else f"_{path}")] = rec
         result["sub"] = sub
