@@ -89,6 +89,24 @@ __device__ __forceinline__ float round_through(float v) {
   return T::to_float(T::from_float(v));
 }
 
+// Unpack 8 values of a 16-bit element type held in a 16-byte vector into FP32 (exact).
+template <typename T>
+__device__ __forceinline__ void unpack8(const uint4& v, float* out);
+template <>
+__device__ __forceinline__ void unpack8<bf16_t>(const uint4& v, float* out) {
+  unpack_bf16x8(v, out);
+}
+template <>
+__device__ __forceinline__ void unpack8<f16_t>(const uint4& v, float* out) {
+  const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __half22float2(h[i]);
+    out[2 * i] = f.x;
+    out[2 * i + 1] = f.y;
+  }
+}
+
 template <typename I>
 __device__ __forceinline__ int load_index(const void* base, int64_t i) {
   return static_cast<int>(reinterpret_cast<const I*>(base)[i]);

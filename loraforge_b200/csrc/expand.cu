@@ -13,7 +13,12 @@
 // The sub-tile's z values are staged in shared memory as FP32.
 //
 // bgmv_expand_kernel and vllm_expand_kernel serve the padded SGLang and vLLM
-// layouts for FP32/FP16/BF16 activations.
+// layouts for FP32/FP16/BF16 activations, one CTA per (token, 256-column block).
+// Where the element type is 16-bit and the B rows are aligned for 16-byte loads, the
+// same arithmetic runs in *_vec_kernel forms: a CTA walks column blocks for one token
+// with several 16-byte B loads per thread in flight.
+#include <algorithm>
+
 #include "launch.cuh"
 
 namespace lfb {
@@ -283,6 +288,168 @@ __global__ void bgmv_expand_kernel(const typename T::storage* __restrict__ z,
   *yp = T::from_float(T::to_float(*yp) + delta);
 }
 
+// ------------------------------------------------------------------ column walkers
+// The first RQ 16-byte pieces (8 * RQ elements) of one B row and the old output value of one
+// (token, column), loaded ahead of their use.
+template <int RQ>
+struct RowPiece {
+  uint4 w[RQ];
+  float old;
+};
+
+template <typename T, int RQ>
+__device__ __forceinline__ void load_piece(RowPiece<RQ>& p, const typename T::storage* row,
+                                           int count, const typename T::storage* yp, bool live,
+                                           bool read_old = true) {
+  const uint4* v = reinterpret_cast<const uint4*>(row);
+#pragma unroll
+  for (int q = 0; q < RQ; ++q) p.w[q] = live && q * 8 < count ? __ldg(v + q) : make_uint4(0, 0, 0, 0);
+  p.old = live && read_old ? T::to_float(*yp) : 0.f;
+}
+
+// acc = fma(lhs[k], row[k], acc) for k = 0 .. r - 1 in order: the piece's elements first, then
+// the rest of the row (ranks above 8 * RQ) read 8 elements at a time.  An FMA's product is
+// exact before its one rounding, so the operand order does not change the result.
+template <typename T, int RQ>
+__device__ __forceinline__ float row_products(const RowPiece<RQ>& p, const typename T::storage* row,
+                                              const float* lhs, int r) {
+  float acc = 0.f;
+#pragma unroll
+  for (int q = 0; q < RQ; ++q) {
+    float b[8];
+    unpack8<T>(p.w[q], b);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (8 * q + j < r) acc = fmaf(lhs[8 * q + j], b[j], acc);
+  }
+  const uint4* v = reinterpret_cast<const uint4*>(row);
+  for (int k0 = 8 * RQ; k0 < r; k0 += 8) {
+    float b[8];
+    unpack8<T>(__ldg(v + k0 / 8), b);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (k0 + j < r) acc = fmaf(lhs[k0 + j], b[j], acc);
+  }
+  return acc;
+}
+
+// The staged z (or v) values of one slice, held in registers by a walker thread and reloaded
+// from shared memory only when its column moves into another slice, so the products read no
+// shared memory.  Used for rows of up to 32 elements (RQ <= 4).
+template <int RQ>
+struct HeldSlice {
+  float v[8 * RQ];
+  int slice = -1;
+
+  __device__ __forceinline__ void select(int s, const float* values, int r) {
+    if (s == slice) return;
+    slice = s;
+#pragma unroll
+    for (int k = 0; k < 8 * RQ; ++k) v[k] = k < r ? values[k] : 0.f;
+  }
+};
+
+// row_products with the left-hand values held in registers and the whole row in the piece
+// (r <= 8 * RQ); full-length rows skip the per-element rank test.
+template <typename T, int RQ>
+__device__ __forceinline__ float held_products(const RowPiece<RQ>& p, const HeldSlice<RQ>& h,
+                                               int r) {
+  float acc = 0.f;
+  if (r == 8 * RQ) {
+#pragma unroll
+    for (int q = 0; q < RQ; ++q) {
+      float b[8];
+      unpack8<T>(p.w[q], b);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc = fmaf(h.v[8 * q + j], b[j], acc);
+    }
+  } else {
+#pragma unroll
+    for (int q = 0; q < RQ; ++q) {
+      float b[8];
+      unpack8<T>(p.w[q], b);
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (8 * q + j < r) acc = fmaf(h.v[8 * q + j], b[j], acc);
+    }
+  }
+  return acc;
+}
+
+// RQ for a row capacity that is a multiple of 8: the whole row when it has at most 64 elements.
+inline int row_pieces(int64_t elems) { return elems <= 8 ? 1 : elems <= 16 ? 2 : elems <= 32 ? 4 : 8; }
+
+// Pieces in flight per thread: the next column's.  Rings of 2 and 4 pieces (more registers,
+// fewer resident CTAs) measured slower on the decode shapes.
+template <int RQ>
+constexpr int ring_depth() { return 1; }
+
+// Column walkers: about kWalkersPerSm CTAs per SM over all tokens (4 to 16 measured level on
+// the decode shapes, 32 slower).
+constexpr int kWalkersPerSm = 8;
+
+// bgmv_expand_kernel's arithmetic for 16-bit elements whose B rows are 16-byte aligned and a
+// multiple of 8 elements long, with unit column stride.  A CTA stages its token's z once and
+// walks the column blocks blockIdx.y, blockIdx.y + gridDim.y, ...; each thread keeps the B
+// rows and old output values of its next D columns in flight (a ring of D pieces in
+// registers, each refilled as soon as it is used), read as 16-byte vectors, and holds the z
+// values of its column's slice in registers.  The chain of dependent loads (route, rank, z)
+// is paid once per CTA instead of once per 256 columns.
+template <typename T, typename I, typename OI, typename SC, int RQ>
+__global__ void __launch_bounds__(256)
+bgmv_expand_vec_kernel(const typename T::storage* __restrict__ z,
+                       const typename T::storage* __restrict__ B, const void* ranks,
+                       const typename SC::storage* scales, const void* map, const void* offsets,
+                       typename T::storage* y, int64_t ys0, int N, int num_slots, int S, int rmax) {
+  using St = typename T::storage;
+  constexpr int D = ring_depth<RQ>();
+  extern __shared__ float zt[];  // S * rmax
+  __shared__ int offs[17];
+  const int t = blockIdx.x;
+  const int g = load_index<I>(map, t);
+  if (g < 0 || g >= num_slots) return;
+  const int r = min(load_index<I>(ranks, g), rmax);
+  if (r <= 0) return;
+  const St* bslot = B + int64_t(g) * N * rmax;
+  St* yrow = y + int64_t(t) * ys0;
+  const int step = gridDim.y * blockDim.x;
+  const int first = blockIdx.y * blockDim.x + threadIdx.x;
+  RowPiece<RQ> ring[D];
+  const auto fetch = [&](RowPiece<RQ>& p, int col, bool live) {
+    const int c = min(col, N - 1);
+    load_piece<T, RQ>(p, bslot + int64_t(c) * rmax, r, yrow + c, live && col < N);
+  };
+#pragma unroll
+  for (int d = 0; d < D; ++d) fetch(ring[d], first + d * step, true);
+  for (int i = threadIdx.x; i < S * r; i += blockDim.x)
+    zt[i] = T::to_float(z[int64_t(t) * S * rmax + i]);
+  for (int i = threadIdx.x; i <= S && i < 17; i += blockDim.x) offs[i] = load_index<OI>(offsets, i);
+  __syncthreads();
+  const int lo = max(offs[0], 0), hi = min(offs[S], N);
+  const float scale = SC::to_float(scales[g]);
+  int s = 0;  // slice of the thread's column: its columns only increase
+  HeldSlice<(RQ <= 4 ? RQ : 1)> held;
+  for (int n = first; n < hi; n += D * step) {  // no barrier below: threads leave independently
+#pragma unroll
+    for (int d = 0; d < D; ++d) {
+      const int col = n + d * step;
+      if (col >= lo && col < hi) {
+        while (s + 1 < S && col >= offs[s + 1]) ++s;
+        float acc;
+        if constexpr (RQ <= 4) {
+          held.select(s, zt + s * r, r);
+          acc = held_products<T, RQ>(ring[d], held, r);
+        } else {
+          acc = row_products<T, RQ>(ring[d], bslot + int64_t(col) * rmax, zt + s * r, r);
+        }
+        yrow[col] = T::from_float(ring[d].old + round_through<T>(acc * scale));
+      }
+      const int ahead = col + D * step;
+      fetch(ring[d], ahead, ahead >= lo && ahead < hi);
+    }
+  }
+}
+
 // ------------------------------------------------------------------ vLLM expand
 struct VllmSlices {
   lf_slice_desc d[8];
@@ -318,6 +485,81 @@ __global__ void vllm_expand_kernel(const float* __restrict__ v, const __grid_con
   *yp = T::from_float(acc);
 }
 
+// vllm_expand_kernel's arithmetic for 16-bit elements whose slices all have 16-byte aligned
+// bases and slot / row strides of a multiple of 8 elements, as a column walker with a ring of
+// D pieces in flight per thread and the slice's v values held in registers (see
+// bgmv_expand_vec_kernel).
+template <typename T, int RQ>
+__global__ void __launch_bounds__(256)
+vllm_expand_vec_kernel(const float* __restrict__ v, const __grid_constant__ VllmSlices sl, int S,
+                       int R, typename T::storage* y, int64_t y_stride,
+                       const int32_t* __restrict__ routes, int T_tokens, int num_slots,
+                       int64_t offset, int add) {
+  using St = typename T::storage;
+  constexpr int D = ring_depth<RQ>();
+  extern __shared__ float vt[];  // S * R
+  const int t = blockIdx.x;
+  const int g = routes[t];
+  if (g < 0 || g >= num_slots) return;
+  const int64_t total = sl.begin[S];
+  St* yrow = y + int64_t(t) * y_stride + offset;
+  const auto row_of = [&](int64_t col, int& s) {
+    s = 0;
+    while (s + 1 < S && col >= sl.begin[s + 1]) ++s;
+    return reinterpret_cast<const St*>(sl.d[s].ptr) + int64_t(g) * sl.d[s].slot_stride +
+           (col - sl.begin[s]) * sl.d[s].row_stride;
+  };
+  const auto fetch = [&](RowPiece<RQ>& p, int64_t col) {
+    const int64_t c = min(col, total - 1);
+    int s;
+    load_piece<T, RQ>(p, row_of(c, s), R, yrow + c, col < total, add != 0);
+  };
+  const int64_t step = int64_t(gridDim.y) * blockDim.x;
+  const int64_t first = int64_t(blockIdx.y) * blockDim.x + threadIdx.x;
+  RowPiece<RQ> ring[D];
+#pragma unroll
+  for (int d = 0; d < D; ++d) fetch(ring[d], first + d * step);
+  for (int i = threadIdx.x; i < S * R; i += blockDim.x) {
+    const int si = i / R, k = i - si * R;
+    vt[i] = v[(int64_t(si) * T_tokens + t) * R + k];
+  }
+  __syncthreads();
+  HeldSlice<(RQ <= 4 ? RQ : 1)> held;
+  for (int64_t n = first; n < total; n += D * step) {  // no barrier below
+#pragma unroll
+    for (int d = 0; d < D; ++d) {
+      const int64_t col = n + d * step;
+      if (col < total) {
+        int s;
+        const St* row = row_of(col, s);
+        float acc;
+        if constexpr (RQ <= 4) {
+          held.select(s, vt + s * R, R);
+          acc = held_products<T, RQ>(ring[d], held, R);
+        } else {
+          acc = row_products<T, RQ>(ring[d], row, vt + s * R, R);
+        }
+        if (add) acc += ring[d].old;
+        yrow[col] = T::from_float(acc);
+      }
+      fetch(ring[d], col + D * step);
+    }
+  }
+}
+
+// Column-block walkers per token for the *_vec_kernel forms: about eight CTAs per SM over all
+// tokens, at most one per column block.
+inline unsigned column_walkers(int64_t tokens, unsigned column_blocks) {
+  static int sms[64] = {};
+  int device = 0;
+  cudaGetDevice(&device);
+  int& count = sms[device & 63];
+  if (count == 0) cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, device);
+  const int64_t want = (int64_t(std::max(count, 1)) * kWalkersPerSm + tokens - 1) /
+                       std::max<int64_t>(tokens, 1);
+  return unsigned(std::max<int64_t>(1, std::min<int64_t>(want, column_blocks)));
+}
+
 template <typename T, typename I, typename OI, typename SC>
 int launch_bgmv_expand(const void* z, const void* b, const void* ranks, const void* scales,
                        const void* map, const void* offsets, void* y, int64_t ys0, int64_t ys1,
@@ -326,13 +568,27 @@ int launch_bgmv_expand(const void* z, const void* b, const void* ranks, const vo
   using St = typename T::storage;
   const dim3 grid(unsigned(T_tokens), unsigned((N + 255) / 256));
   const size_t smem = sizeof(float) * size_t(S) * rmax;
-  static int flags[64] = {};
-  auto kernel = bgmv_expand_kernel<T, I, OI, SC>;
-  if (int rc = ensure_smem(kernel, int(smem), flags)) return rc;
-  kernel<<<grid, 256, smem, stream>>>(static_cast<const St*>(z), static_cast<const St*>(b),
-                                      ranks, static_cast<const typename SC::storage*>(scales),
-                                      map, offsets, static_cast<St*>(y), ys0, ys1, N, num_slots,
-                                      S, rmax);
+  // S * rmax <= 16 * 256 FP32 values: always within the default 48 KiB of shared memory.
+  if constexpr (sizeof(St) == 2) {
+    if (rmax % 8 == 0 && ys1 == 1 && aligned16(b)) {
+      auto kernel = bgmv_expand_vec_kernel<T, I, OI, SC, 8>;
+      switch (row_pieces(rmax)) {
+        case 1: kernel = bgmv_expand_vec_kernel<T, I, OI, SC, 1>; break;
+        case 2: kernel = bgmv_expand_vec_kernel<T, I, OI, SC, 2>; break;
+        case 4: kernel = bgmv_expand_vec_kernel<T, I, OI, SC, 4>; break;
+      }
+      const dim3 vgrid(unsigned(T_tokens), column_walkers(T_tokens, grid.y));
+      kernel<<<vgrid, 256, smem, stream>>>(
+          static_cast<const St*>(z), static_cast<const St*>(b), ranks,
+          static_cast<const typename SC::storage*>(scales), map, offsets, static_cast<St*>(y),
+          ys0, N, num_slots, S, rmax);
+      return check_launch("bgmv_expand");
+    }
+  }
+  bgmv_expand_kernel<T, I, OI, SC><<<grid, 256, smem, stream>>>(
+      static_cast<const St*>(z), static_cast<const St*>(b), ranks,
+      static_cast<const typename SC::storage*>(scales), map, offsets, static_cast<St*>(y), ys0,
+      ys1, N, num_slots, S, rmax);
   return check_launch("bgmv_expand");
 }
 
@@ -371,6 +627,22 @@ int bgmv_expand_t(int32_t scale_dtype, const void* z, const void* b, const void*
                                                ys0, ys1, T_tokens, N, num_slots, S, rmax, stream);
   return bgmv_expand_sc<T, int64_t, int64_t>(scale_dtype, z, b, ranks, scales, map, offsets, y,
                                              ys0, ys1, T_tokens, N, num_slots, S, rmax, stream);
+}
+
+template <typename T>
+int launch_vllm_vec(dim3 grid, size_t smem, cudaStream_t s, const float* v, const VllmSlices& sl,
+                    int num_slices, int rank, void* y, int64_t y_stride, const int32_t* routes,
+                    int64_t num_tokens, int num_slots, int64_t offset, int add) {
+  auto kernel = vllm_expand_vec_kernel<T, 8>;
+  switch (row_pieces(rank)) {
+    case 1: kernel = vllm_expand_vec_kernel<T, 1>; break;
+    case 2: kernel = vllm_expand_vec_kernel<T, 2>; break;
+    case 4: kernel = vllm_expand_vec_kernel<T, 4>; break;
+  }
+  const dim3 vgrid(grid.x, column_walkers(num_tokens, grid.y));
+  kernel<<<vgrid, 256, smem, s>>>(v, sl, num_slices, rank, static_cast<typename T::storage*>(y),
+                                  y_stride, routes, int(num_tokens), num_slots, offset, add);
+  return check_launch("vllm_expand");
 }
 
 }  // namespace
@@ -473,6 +745,10 @@ extern "C" int lf_vllm_expand(int32_t dtype, const float* v, const lf_slice_desc
   const dim3 grid(unsigned(num_tokens), unsigned((total + 255) / 256));
   const size_t smem = sizeof(float) * size_t(num_slices) * rank;
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  bool vec = rank % 8 == 0;  // 16-byte B pieces: aligned bases, strides of 8 elements
+  for (int i = 0; i < num_slices; ++i)
+    vec = vec && aligned16(sl.d[i].ptr) && sl.d[i].slot_stride % 8 == 0 &&
+          sl.d[i].row_stride % 8 == 0;
   switch (dtype) {
     case LF_F32:
       vllm_expand_kernel<f32_t><<<grid, 256, smem, s>>>(v, sl, num_slices, rank,
@@ -480,11 +756,17 @@ extern "C" int lf_vllm_expand(int32_t dtype, const float* v, const lf_slice_desc
                                                         int(num_tokens), num_slots, offset, add);
       break;
     case LF_F16:
+      if (vec)
+        return launch_vllm_vec<f16_t>(grid, smem, s, v, sl, num_slices, rank, y, y_stride, routes,
+                                      num_tokens, num_slots, offset, add);
       vllm_expand_kernel<f16_t><<<grid, 256, smem, s>>>(v, sl, num_slices, rank,
                                                         static_cast<__half*>(y), y_stride, routes,
                                                         int(num_tokens), num_slots, offset, add);
       break;
     case LF_BF16:
+      if (vec)
+        return launch_vllm_vec<bf16_t>(grid, smem, s, v, sl, num_slices, rank, y, y_stride, routes,
+                                       num_tokens, num_slots, offset, add);
       vllm_expand_kernel<bf16_t><<<grid, 256, smem, s>>>(
           v, sl, num_slices, rank, static_cast<__nv_bfloat16*>(y), y_stride, routes,
           int(num_tokens), num_slots, offset, add);

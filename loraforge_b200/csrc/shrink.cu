@@ -345,23 +345,6 @@ inline int k_parts(int64_t K) {
 constexpr int kTokWarps = 8;
 constexpr int kTokThreads = kTokWarps * 32;
 
-template <typename T>
-__device__ __forceinline__ void unpack8(const uint4& v, float* out);
-template <>
-__device__ __forceinline__ void unpack8<bf16_t>(const uint4& v, float* out) {
-  unpack_bf16x8(v, out);
-}
-template <>
-__device__ __forceinline__ void unpack8<f16_t>(const uint4& v, float* out) {
-  const __half2* h = reinterpret_cast<const __half2*>(&v);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 f = __half22float2(h[i]);
-    out[2 * i] = f.x;
-    out[2 * i + 1] = f.y;
-  }
-}
-
 template <typename T, typename L>
 __global__ void __launch_bounds__(kTokThreads)
 token_shrink_kernel(const __grid_constant__ L layout, const typename T::storage* __restrict__ x,

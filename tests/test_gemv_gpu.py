@@ -130,3 +130,29 @@ def test_int32_metadata_and_aligned_vector_path():
     out = lora_expand(z, b, ranks, scales, routes, offsets, 4096, base)
     torch.testing.assert_close(out, expected, rtol=2e-2, atol=2e-2)
     assert np.isfinite(out.float().cpu().numpy()).all()
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("capacity", [8, 16, 32, 64, 128])
+@pytest.mark.parametrize("tokens", [3, 300])
+def test_vector_expand_matches_scalar_form(dtype, capacity, tokens):
+    # Unit-stride output rows take the 16-byte-vector walker kernel, a column-major output the
+    # element-wise one; both do the same arithmetic, so the outputs agree bit for bit.
+    g = torch.Generator().manual_seed(capacity * 7 + tokens)
+    sizes = [1000, 2500, 777]
+    width = sum(sizes)
+    z = (torch.randn(tokens, 3 * capacity, generator=g) / 4).to(dtype).cuda()
+    b = (torch.randn(5, width, capacity, generator=g) / 4).to(dtype).cuda()
+    ranks = torch.tensor([capacity, 0, max(1, capacity // 2), 3, capacity], device="cuda")
+    routes = torch.randint(-1, 5, (tokens,), generator=g).cuda()
+    scales = torch.tensor([0.5, 1.0, 2.0, 0.25, 1.5], device="cuda")
+    offsets = torch.tensor([0, 1000, 3500, width], device="cuda")
+    base = (torch.randn(tokens, width, generator=g) / 4).to(dtype).cuda()
+    vec = lora_expand(z, b, ranks, scales, routes, offsets, max(sizes), base.clone())
+    column_major = base.t().contiguous().t()
+    assert column_major.stride(1) != 1
+    scalar = lora_expand(z, b, ranks, scales, routes, offsets, max(sizes), column_major)
+    assert torch.equal(vec, scalar)
+    assert torch.equal(vec[routes < 0], base[routes < 0])
+    if (routes == 0).any():
+        assert not torch.equal(vec[routes == 0], base[routes == 0])

@@ -72,3 +72,32 @@ def test_deterministic_shrink_and_base_routes_zero():
         shrink(x, a, again, routes, scale=0.5)
         torch.testing.assert_close(again, first, rtol=0, atol=0)
     assert not first[:, routes < 0].any()
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("rank", [8, 16, 32, 64, 128])
+@pytest.mark.parametrize("add", [False, True])
+@pytest.mark.parametrize("tokens", [3, 300])
+def test_vector_expand_matches_scalar_form(dtype, rank, add, tokens):
+    # Slices with row strides of a multiple of 8 elements take the 16-byte-vector walker
+    # kernel; the same values in rows padded by one element take the element-wise one.  Same
+    # arithmetic, so the outputs agree bit for bit.
+    g = torch.Generator().manual_seed(rank + (1 if add else 0) + tokens)
+    sizes = [1000, 2500, 777]
+    b = [(torch.randn(6, 1, n, rank, generator=g) / 4).to(dtype).cuda() for n in sizes]
+    padded = []
+    for w in b:
+        p = torch.zeros(6, 1, w.shape[2], rank + 1, dtype=dtype, device="cuda")[..., :rank]
+        p.copy_(w)
+        assert p.stride(-2) % 8 != 0
+        padded.append(p)
+    v = (torch.randn(3, tokens, rank, generator=g) / 4).cuda()
+    routes = torch.randint(-1, 6, (tokens,), generator=g, dtype=torch.int32).cuda()
+    y = (torch.randn(tokens, sum(sizes) + 9, generator=g) / 4).to(dtype).cuda()
+    vec, scalar = y.clone(), y.clone()
+    expand(v, b, vec, routes, offset=5, add=add)
+    expand(v, padded, scalar, routes, offset=5, add=add)
+    assert torch.equal(vec, scalar)
+    assert torch.equal(vec[routes < 0], y[routes < 0])
+    end = 5 + sum(sizes)
+    assert torch.equal(vec[:, :5], y[:, :5]) and torch.equal(vec[:, end:], y[:, end:])
