@@ -19,7 +19,9 @@ and the reference's own CUDA row kernels on config 1 (built for sm_100a into ora
 bar on the same box),
 and on config 3 the base projection with the LoRA delta in one GEMM (lora_base_gemm) next to
 cuBLAS's base GEMM followed by lora_shrink_expand_prefill, each timed the same way with its
-own roofline, e2e, CPU baseline and output check.
+own roofline, e2e, CPU baseline and output check.  The sub-records are measured in a random
+order drawn from ``--seed`` (``sub_order``) and reported in a fixed one; each record carries
+the L2-flushed time and ``warm_ms_per_step``, the median of five unflushed trials.
 
 ``value``   tokens/s of the step replayed as a CUDA graph with inputs resident in HBM
             (L2 flushed by a 256 MiB write before every timed step, outside the step's
@@ -45,6 +47,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import random
 import statistics
 import threading
 import time
@@ -907,12 +910,19 @@ def main(argv=None):
     }
     result.update(head)
     if world == 1 and args.config == 4 and not args.no_sub and not args.profile:
-        sub = {}
-        for config, path in ((1, "fused"), (2, "fused"), (3, "fused"), (1, "rows"), (1, "reference_cuda"),
-                             (1, "bgmv"), (1, "vllm"), (3, "base_gemm"), (3, "base_cublas")):
-            rec = measure(config, args, world, rank, local, path, sub=True)
-            sub[f"config{config}" + ("" if path == "fused" else f"_{path}")] = rec
-        result["sub"] = sub
+        variants = [(1, "fused"), (2, "fused"), (3, "fused"), (1, "rows"), (1, "reference_cuda"),
+                    (1, "bgmv"), (1, "vllm"), (3, "base_gemm"), (3, "base_cublas")]
+        names = [f"config{c}" + ("" if path == "fused" else f"_{path}") for c, path in variants]
+        # Measured in a seeded random order, so that no variant always runs right after the
+        # same neighbour (warm clocks, L2 contents, allocator state); reported in fixed order.
+        order = list(range(len(variants)))
+        random.Random(args.seed).shuffle(order)
+        measured = {}
+        for i in order:
+            config, path = variants[i]
+            measured[names[i]] = measure(config, args, world, rank, local, path, sub=True)
+        result["sub"] = {name: measured[name] for name in names}
+        result["sub_order"] = [names[i] for i in order]
     if rank == 0:
         print(json.dumps(result), flush=True)
     if world > 1:
