@@ -850,7 +850,12 @@ def measure(config, args, world, rank, local, path="fused", sub=False):
             "peak": peak,
             "unit": "TFLOP/s" if kind == "gemm" else "GB/s",
             "frac": achieved / peak,
-            "peak_source": f"{peak_kind} (MEASURED_PEAKS.json {'bf16_tflops' if kind == 'gemm' else 'hbm_gbs'})",
+            "peak_source": (
+                f"measured (MEASURED_PEAKS.json {'bf16_tflops' if kind == 'gemm' else 'hbm_gbs'})"
+                if peak_kind == "measured"
+                else "fallback (no MEASURED_PEAKS.json: earlier measurement on this pool, "
+                + ("1.59 PFLOP/s cuBLAS BF16 burst)" if kind == "gemm" else "6.65 TB/s copy)")
+            ),
             "alg_flops" if kind == "gemm" else "alg_bytes": alg,
             "traffic": TRAFFIC.get((config, path, dominant)),
         },
