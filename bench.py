@@ -27,7 +27,9 @@ the L2-flushed time and ``warm_ms_per_step``, the median of five unflushed trial
             (L2 flushed by a 256 MiB write before every timed step, outside the step's
             CUDA events), total time of exactly K steps, max over ranks.
 ``e2e``     the same step through the public Python API with pinned host buffers: H2D of
-            the step's activations and routing, D2H of every output, per step.
+            the step's activations and routing, D2H of every output, per step; copies on
+            their own streams with double-buffered inputs and outputs, so one step's copies
+            overlap its neighbours' kernels.
 ``roofline`` the dominant call's algorithmic bytes / its mean CUDA-event time against the
             measured HBM copy bandwidth (MEASURED_PEAKS.json), with its ncu DRAM traffic.
 ``cpu_baseline`` the FP32 einsum over per-adapter gathers (the oracle port of the
@@ -669,32 +671,74 @@ def time_graph(w, steps, warmup, flush, world=1):
 
 
 def time_e2e(w, steps, warmup):
-    """Public API with host buffers: H2D inputs, the step, D2H outputs, per step."""
+    """Public API with host buffers: H2D inputs, the step, D2H outputs, every step.
+
+    Served steps are pipelined the way an engine runs them: the inputs and outputs are double
+    buffered on the device and in pinned host memory, the H2D copies run on one stream, the
+    step on the current stream and the D2H copies on a third, so step i's D2H and step i+1's
+    H2D overlap step i+1's kernels.  Every step still copies all of its inputs in and all of its
+    outputs out; the time is from the first copy to the last byte back.
+    """
     import torch
 
-    host_x = {k: v.cpu().pin_memory() for k, v in w.x.items()}
-    host_slots = w.slots.cpu().pin_memory()
-    host_out = [torch.empty(p.y.shape, dtype=p.y.dtype).pin_memory() for p in w.projections]
+    compute = torch.cuda.current_stream()
+    h2d_stream, d2h_stream = torch.cuda.Stream(), torch.cuda.Stream()
+    own_x, own_slots = w.x, w.slots
+    own_y = [p.y for p in w.projections]
+    dev_x = [own_x, {k: torch.empty_like(v) for k, v in own_x.items()}]
+    dev_slots = [own_slots, torch.empty_like(own_slots)]
+    dev_y = [own_y, [torch.empty_like(y).copy_(y) for y in own_y]]
+    host_x = {k: v.cpu().pin_memory() for k, v in own_x.items()}
+    host_slots = own_slots.cpu().pin_memory()
+    host_out = [[torch.empty(y.shape, dtype=y.dtype).pin_memory() for y in own_y] for _ in range(2)]
     h2d = sum(t.numel() * 2 for t in host_x.values()) + host_slots.numel() * 4
-    d2h = sum(t.numel() * 2 for t in host_out)
+    d2h = sum(t.numel() * 2 for t in host_out[0])
+    inputs_used = [None, None]  # step done with buffer b's inputs (next H2D into b waits)
+    outputs_read = [None, None]  # D2H done with buffer b's outputs (next step into b waits)
 
-    def one():
-        for k, t in host_x.items():
-            w.x[k].copy_(t, non_blocking=True)
-        w.slots.copy_(host_slots, non_blocking=True)
+    def one(i):
+        b = i % 2
+        with torch.cuda.stream(h2d_stream):
+            if inputs_used[b] is not None:
+                h2d_stream.wait_event(inputs_used[b])
+            for k, t in host_x.items():
+                dev_x[b][k].copy_(t, non_blocking=True)
+            dev_slots[b].copy_(host_slots, non_blocking=True)
+            landed = torch.cuda.Event()
+            landed.record(h2d_stream)
+        compute.wait_event(landed)
+        if outputs_read[b] is not None:
+            compute.wait_event(outputs_read[b])
+        w.x, w.slots = dev_x[b], dev_slots[b]
+        for p, y in zip(w.projections, dev_y[b]):
+            p.y = y
         run_step(w)
-        for p, h in zip(w.projections, host_out):
-            h.copy_(p.y, non_blocking=True)
+        done = torch.cuda.Event()
+        done.record(compute)
+        inputs_used[b] = done
+        with torch.cuda.stream(d2h_stream):
+            d2h_stream.wait_event(done)
+            for y, h in zip(dev_y[b], host_out[b]):
+                h.copy_(y, non_blocking=True)
+            read = torch.cuda.Event()
+            read.record(d2h_stream)
+        outputs_read[b] = read
 
-    for _ in range(warmup):
-        one()
-    torch.cuda.synchronize()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record()
-    for _ in range(steps):
-        one()
-    end.record()
-    torch.cuda.synchronize()
+    try:
+        for i in range(warmup):
+            one(i)
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(h2d_stream)
+        for i in range(steps):
+            one(i)
+        compute.wait_stream(d2h_stream)
+        end.record(compute)
+        torch.cuda.synchronize()
+    finally:
+        w.x, w.slots = own_x, own_slots
+        for p, y in zip(w.projections, own_y):
+            p.y = y
     return start.elapsed_time(end) / steps, h2d, d2h
 
 
