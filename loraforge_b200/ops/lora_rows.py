@@ -4,9 +4,9 @@ These keep the public surface of ``loraforge.ops.lora_rows``
 (src/loraforge/ops/lora_rows.py:54-239): the call signatures and keyword names, the
 order in which arguments are checked, and the exception types and message texts.  The
 checks read tensor metadata only, so a call never waits for the GPU and a warmed call can
-be recorded into a CUDA graph.  The work runs in ``lf_row_shrink`` (adapter-major: each
-touched slot's A rows are read once per tile of its tokens) and ``lf_row_expand`` (the
-reference's element arithmetic, so equal inputs give equal bits).
+be recorded into a CUDA graph.  The work runs in ``lf_row_shrink`` (one warp per token and
+rank row, summed in the reference kernel's order, so z matches it bit for bit) and
+``lf_row_expand`` (the reference's element arithmetic, so equal inputs give equal bits).
 """
 
 from __future__ import annotations
