@@ -931,6 +931,24 @@ def measure(config, args, world, rank, local, path="fused", sub=False):
     return record
 
 
+# ----------------------------------------------------------------------------- sub-records
+SUB_RECORDS = ((1, "fused"), (2, "fused"), (3, "fused"), (1, "rows"), (1, "reference_cuda"),
+               (1, "bgmv"), (1, "vllm"), (3, "base_gemm"), (3, "base_cublas"))
+
+
+def sub_record_name(config, path):
+    return f"config{config}" + ("" if path == "fused" else f"_{path}")
+
+
+def sub_record_order(seed):
+    """Indices of SUB_RECORDS in measurement order: a random order drawn from ``seed``, so that
+    no variant always runs right after the same neighbour (warm clocks, L2 contents, allocator
+    state); the line reports them in the fixed order."""
+    order = list(range(len(SUB_RECORDS)))
+    random.Random(seed).shuffle(order)
+    return order
+
+
 # ----------------------------------------------------------------------------- main
 def main(argv=None):
     args = parse_args(argv)
@@ -959,13 +977,9 @@ def main(argv=None):
     }
     result.update(head)
     if world == 1 and args.config == 4 and not args.no_sub and not args.profile:
-        variants = [(1, "fused"), (2, "fused"), (3, "fused"), (1, "rows"), (1, "reference_cuda"),
-                    (1, "bgmv"), (1, "vllm"), (3, "base_gemm"), (3, "base_cublas")]
-        names = [f"config{c}" + ("" if path == "fused" else f"_{path}") for c, path in variants]
-        # Measured in a seeded random order, so that no variant always runs right after the
-        # same neighbour (warm clocks, L2 contents, allocator state); reported in fixed order.
-        order = list(range(len(variants)))
-        random.Random(args.seed).shuffle(order)
+        variants = SUB_RECORDS
+        names = [sub_record_name(c, path) for c, path in variants]
+        order = sub_record_order(args.seed)
         measured = {}
         for i in order:
             config, path = variants[i]

@@ -56,3 +56,12 @@ def test_reference_arm_never_loads_the_package():
     assert line["impl"] == "reference" and line["value"] > 0
     assert line["config"] == bench.config_record(2, 1)
     assert line["e2e"]["h2d_bytes_per_step"] == 0
+
+
+def test_sub_records_run_in_a_seeded_random_order():
+    first, again, other = (bench.sub_record_order(seed) for seed in (1234, 1234, 7))
+    assert sorted(first) == list(range(len(bench.SUB_RECORDS)))
+    assert first == again
+    assert first != other or len(first) < 3
+    names = [bench.sub_record_name(c, p) for c, p in bench.SUB_RECORDS]
+    assert len(set(names)) == len(names) and "config1" in names and "config1_bgmv" in names
