@@ -3,8 +3,9 @@
 Keeps the surface of ``loraforge.ops.vllm_gemv`` (src/loraforge/ops/vllm_gemv.py:49-159):
 signatures, checks and messages; torch is imported only when a call is made.  The
 reference's shrink splits K across programs that add with FP32 atomics, so its low bits
-vary run to run; here the K split is summed in a fixed order within one thread-block
-cluster, and repeated calls give identical bits.  A route of -1 gives a zero intermediate
+vary run to run; here every (token, rank row) sum runs in a fixed order (one warp per row,
+or, for FP32 and unaligned operands, a K split over one thread-block cluster added in rank
+order), and repeated calls give identical bits.  A route of -1 gives a zero intermediate
 row and leaves the output row as it was.
 """
 
