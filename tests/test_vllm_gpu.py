@@ -2,7 +2,8 @@
 
 Mirrors test_raw_gemv of tests/test_vllm_gpu.py in lishenghui/loraforge against
 golden outputs of the reference's FP64 oracle, plus determinism (the reference's
-split-K atomics are replaced by a fixed-order cluster reduction).
+split-K atomics are replaced by sums in a fixed order) and bit identity of the walker
+and element-wise expand kernels.
 """
 
 import pytest
