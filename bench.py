@@ -70,6 +70,8 @@ TRAFFIC = {
     (1, "fused", "gate_up_proj.fused"): (19.434496 + 75.373056 + 0.404224) * 1e6,
     (2, "fused", "proj.fused"): (51.122176 + 0.006656 + 49.678592 + 0.019456) * 1e6,
     (4, "fused", "gate_up_proj.fused"): (145.565696 + 0.168192 + 820.420352 + 53.785344) * 1e6,
+    (1, "bgmv", "gate_up_proj.expand"): (75.263232 + 1.180416) * 1e6,
+    (1, "vllm", "gate_up_proj.expand"): (75.279104 + 1.009920) * 1e6,
 }
 
 
